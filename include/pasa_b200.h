@@ -1,0 +1,158 @@
+/*
+ * pasa_b200 — C ABI of the B200 (sm_100a) precision-allocated sparse
+ * attention forward.
+ *
+ * The reference implementation is ZHANGWENTAI/PASA
+ * svg/kernels/triton/group_pisa_attention.py.  Each entry point below names
+ * the reference interface it replaces.  Conventions shared by all entry
+ * points:
+ *
+ *   - every pointer is a device pointer owned by the caller, except where a
+ *     parameter says "host";
+ *   - tensors are dense and row-major; q, k, v, o are [B*H, T, D];
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); nothing
+ *     synchronises the stream and nothing allocates device memory;
+ *   - the return value is a pasa_status (0 = success); a non-zero status
+ *     means no kernel was launched, except PASA_ERR_CUDA, which reports a
+ *     launch failure of the CUDA runtime.
+ *
+ * Supported: dtype bf16 or fp32, head_dim 64 or 128, block 64, group 32.
+ */
+#ifndef PASA_B200_H
+#define PASA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PASA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PASA_API __attribute__((visibility("default")))
+#else
+#define PASA_API
+#endif
+
+typedef enum pasa_status {
+  PASA_OK = 0,
+  PASA_ERR_SHAPE = 1,      /* a size or count is out of range            */
+  PASA_ERR_DTYPE = 2,      /* unsupported element type                   */
+  PASA_ERR_ALIGN = 3,      /* a pointer is not 16-byte aligned           */
+  PASA_ERR_DENSITY = 4,    /* density outside (0, 1] or not finite       */
+  PASA_ERR_UNSUPPORTED = 5,/* head_dim / block / group not supported     */
+  PASA_ERR_WORKSPACE = 6,  /* workspace missing or too small             */
+  PASA_ERR_NULL = 7,       /* a required pointer is NULL                 */
+  PASA_ERR_CUDA = 8,       /* the CUDA runtime reported an error         */
+  PASA_ERR_DEVICE = 9      /* the device is not an sm_100 GPU            */
+} pasa_status;
+
+typedef enum pasa_dtype {
+  PASA_BF16 = 0,
+  PASA_F32 = 1
+} pasa_dtype;
+
+/* Attention kernel selection for pasa_attn / pasa_forward. */
+typedef enum pasa_attn_kernel {
+  PASA_ATTN_AUTO = 0,     /* tcgen05 kernel for bf16, CUDA-core kernel for fp32 */
+  PASA_ATTN_TCGEN05 = 1,  /* bf16 only: TMA + tcgen05/TMEM pair-tile kernel     */
+  PASA_ATTN_SIMT = 2      /* CUDA-core kernel, one 64-query block per CTA       */
+} pasa_attn_kernel;
+
+/* Bits a kernel may set in the caller's error word (see pasa_attn). */
+#define PASA_DEVERR_WAIT_TIMEOUT 0x1u  /* a bounded barrier wait gave up */
+
+/* ABI version of the loaded library (PASA_ABI_VERSION). */
+PASA_API int pasa_abi_version(void);
+
+/* Static text for a status code. */
+PASA_API const char* pasa_status_string(int status);
+
+/*
+ * Derived sizes: NT = ceil(T / block), NG = ceil(NT / group) and the number
+ * of exactly attended blocks per query block
+ * NS = min(max(1, (int)(density * NT)), NT).
+ * Replaces the host arithmetic of group_pisa_attention.py:345, :294-299, :373.
+ * All outputs are host pointers; any may be NULL.
+ */
+PASA_API int pasa_derive(int64_t T, int block, int group, double density,
+                int64_t* nt, int64_t* ng, int64_t* ns);
+
+/* Bytes of device workspace pasa_forward needs (host output). */
+PASA_API int pasa_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype,
+                        int block, int group, int64_t ns, size_t* bytes);
+
+/*
+ * Block statistics.  Replaces fused_chunk_reduce + compute_h_group
+ * (group_pisa_attention.py:268-301, kernel :75-129):
+ *   qc, kc  [B*H, NG*group, D]  block means (rows >= NT written as zero)
+ *   vc      [B*H, NG*group, D]  block sums  (rows >= NT written as zero)
+ *   h_norm  [B*H, NT]           fp32 Frobenius norm of k^T v - kc (x) vc
+ *   h_group [B*H, NG, D, D]     per-group mean of the per-block matrices
+ * qc, kc, vc, h_group have the input dtype.  The per-block matrices
+ * themselves are never written to memory.
+ */
+PASA_API int pasa_prep(void* stream, const void* q, const void* k, const void* v,
+              int64_t B, int64_t H, int64_t T, int D, int dtype, int block, int group,
+              void* qc, void* kc, void* vc, float* h_norm, void* h_group);
+
+/*
+ * Covariance-aware top-k block selection.  Replaces
+ * group_pisa_attention.py:365-375 (einsum score, log(h_norm + 1e-6) bias,
+ * optional noise, torch.topk):
+ *   indices  [B*H, NT, ns] int32, best first; equal scores by lower index
+ *   sel_mask [B*H, NT, NG] uint32; bit b of word g set when block 32g+b is
+ *            among the row's indices (may be NULL)
+ * qc, kc are as written by pasa_prep (row stride NG*group).  noise
+ * [B*H, NT] fp32 is added to the bias when non-NULL (the reference's
+ * use_random draw).  use_cov_bias = 0 ranks by the dot product alone.
+ */
+PASA_API int pasa_select(void* stream, const void* qc, const void* kc, const float* h_norm,
+                const float* noise, int64_t BH, int64_t NT, int D, int dtype,
+                float scale, int use_cov_bias, int64_t ns,
+                int32_t* indices, uint32_t* sel_mask);
+
+/*
+ * Exact attention over the selected blocks plus the zero-order and per-group
+ * first-order correction over all other blocks, one online-softmax pass.
+ * Replaces pisa_pg_fwd_kernel (group_pisa_attention.py:136-262) and its
+ * launch (:380-396).  o is [B*H, T, D] in the input dtype.  err_word
+ * (nullable, device uint32) receives PASA_DEVERR_* bits.
+ */
+PASA_API int pasa_attn(void* stream, const void* q, const void* k, const void* v,
+              const void* kc, const void* vc, const void* h_group,
+              const int32_t* indices, const uint32_t* sel_mask,
+              int64_t BH, int64_t T, int D, int dtype, float scale, int64_t ns,
+              void* o, uint32_t* err_word, int kernel);
+
+/*
+ * The whole op, pisa_pg_attention(q, k, v, density, ..., scale,
+ * use_cov_bias) (group_pisa_attention.py:307-398) on caller memory:
+ * prep -> select -> attention on `stream`.  workspace must hold
+ * pasa_workspace_size() bytes, 256-byte aligned.  noise as in pasa_select.
+ */
+PASA_API int pasa_forward(void* stream, const void* q, const void* k, const void* v,
+                 int64_t B, int64_t H, int64_t T, int D, int dtype,
+                 double density, float scale, int use_cov_bias, const float* noise,
+                 void* workspace, size_t workspace_bytes, void* o, int kernel);
+
+/*
+ * Token-layout permutation of the temporal heads (frame-major <-> token-
+ * major), text tail untouched.  Replaces hunyuan_sparse_head_placement
+ * (svg/models/hyvideo/placement.py:34-153) when inverse = 0 and
+ * hunyuan_hidden_states_placement (:285-387) when inverse = 1.
+ *   src, dst          [cfg, H, T, D], T = context_length + num_frame*frame_size
+ *   head_is_temporal  [cfg, H] int32 (the best_mask_idx of the reference)
+ * Spatial heads (0) are copied unchanged.  src and dst must not overlap.
+ */
+PASA_API int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal,
+               int64_t cfg, int64_t H, int64_t T, int D, int dtype,
+               int64_t context_length, int64_t num_frame, int64_t frame_size, int inverse);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PASA_B200_H */

@@ -1,0 +1,219 @@
+// extern "C" entry points of libpasa_b200.so: argument validation, the
+// workspace layout, and kernel dispatch.  Declarations and the reference
+// interface each entry point replaces are in include/pasa_b200.h.
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace pasa {
+cudaError_t launch_prep(cudaStream_t, int, int, const void*, const void*, const void*, int64_t, int64_t, void*,
+                        void*, void*, float*, void*);
+cudaError_t launch_select(cudaStream_t, int, int, const void*, const void*, const float*, const float*, int64_t,
+                          int64_t, int64_t, float, int, int32_t*, uint32_t*);
+size_t select_smem_bytes(int D, int64_t NT, int64_t NG, int64_t NS);
+cudaError_t launch_attn_simt(cudaStream_t, int, int, const void*, const void*, const void*, const void*,
+                             const void*, const void*, const int32_t*, const uint32_t*, int64_t, int64_t,
+                             int64_t, float, void*);
+cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const void*, const void*, const void*,
+                           const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*);
+cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
+                         int64_t, int64_t, int64_t, int);
+}  // namespace pasa
+
+using namespace pasa;
+
+namespace {
+
+constexpr size_t kMaxSmem = 227 * 1024;
+
+int esize_of(int dtype) { return dtype == PASA_BF16 ? 2 : 4; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int64_t BH, int64_t T, int D, int dtype) {
+  if (dtype != PASA_BF16 && dtype != PASA_F32) return PASA_ERR_DTYPE;
+  if (D != 64 && D != 128) return PASA_ERR_UNSUPPORTED;
+  if (BH < 1 || T < 1) return PASA_ERR_SHAPE;
+  if (BH > 65535) return PASA_ERR_SHAPE;                     // grid.y
+  const int64_t NT = cdiv(T, kBlock);
+  if (NT > (int64_t(1) << 24)) return PASA_ERR_SHAPE;
+  return PASA_OK;
+}
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PASA_ERR_CUDA;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return PASA_ERR_CUDA;
+  return major == 10 ? PASA_OK : PASA_ERR_DEVICE;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? PASA_OK : PASA_ERR_CUDA; }
+
+int64_t top_k_of(double density, int64_t NT) {
+  // min(max(1, int(density * NT)), NT)   (group_pisa_attention.py:373)
+  const double prod = density * double(NT);
+  int64_t t = (prod >= 9.0e18) ? NT : (prod <= -9.0e18 ? 0 : int64_t(prod));  // int() truncates toward 0
+  if (t < 1) t = 1;
+  if (t > NT) t = NT;
+  return t;
+}
+
+int check_select_fit(int D, int64_t NT, int64_t NS) {
+  const int64_t NG = cdiv(NT, kGroup);
+  return select_smem_bytes(D, NT, NG, NS) <= kMaxSmem ? PASA_OK : PASA_ERR_SHAPE;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pasa_abi_version(void) { return PASA_ABI_VERSION; }
+
+const char* pasa_status_string(int status) {
+  switch (status) {
+    case PASA_OK: return "ok";
+    case PASA_ERR_SHAPE: return "invalid shape or size";
+    case PASA_ERR_DTYPE: return "unsupported dtype (bf16 or fp32 expected)";
+    case PASA_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case PASA_ERR_DENSITY: return "density is not a finite number";
+    case PASA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim 64/128, block 64, group 32)";
+    case PASA_ERR_WORKSPACE: return "workspace missing or too small";
+    case PASA_ERR_NULL: return "required pointer is NULL";
+    case PASA_ERR_CUDA: return "CUDA runtime error";
+    case PASA_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    default: return "unknown status";
+  }
+}
+
+int pasa_derive(int64_t T, int block, int group, double density, int64_t* nt, int64_t* ng, int64_t* ns) {
+  if (block != kBlock || group != kGroup) return PASA_ERR_UNSUPPORTED;
+  if (T < 1) return PASA_ERR_SHAPE;
+  if (!std::isfinite(density)) return PASA_ERR_DENSITY;
+  const int64_t NT = cdiv(T, kBlock);
+  if (nt) *nt = NT;
+  if (ng) *ng = cdiv(NT, kGroup);
+  if (ns) *ns = top_k_of(density, NT);
+  return PASA_OK;
+}
+
+int pasa_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype, int block, int group, int64_t ns,
+                        size_t* bytes) {
+  if (!bytes) return PASA_ERR_NULL;
+  if (block != kBlock || group != kGroup) return PASA_ERR_UNSUPPORTED;
+  if (B < 1 || H < 1) return PASA_ERR_SHAPE;
+  int st = check_common(B * H, T, D, dtype);
+  if (st) return st;
+  const int64_t NT = cdiv(T, kBlock);
+  if (ns < 1 || ns > NT) return PASA_ERR_SHAPE;
+  *bytes = make_layout(B * H, T, D, esize_of(dtype), ns).total;
+  return PASA_OK;
+}
+
+int pasa_prep(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
+              int dtype, int block, int group, void* qc, void* kc, void* vc, float* h_norm, void* h_group) {
+  if (block != kBlock || group != kGroup) return PASA_ERR_UNSUPPORTED;
+  if (B < 1 || H < 1) return PASA_ERR_SHAPE;
+  int st = check_common(B * H, T, D, dtype);
+  if (st) return st;
+  if (!q || !k || !v || !qc || !kc || !vc || !h_norm || !h_group) return PASA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(qc) || !aligned16(kc) || !aligned16(vc) ||
+      !aligned16(h_group))
+    return PASA_ERR_ALIGN;
+  if ((st = check_device())) return st;
+  return cuda_status(launch_prep(static_cast<cudaStream_t>(stream), dtype, D, q, k, v, B * H, T, qc, kc, vc,
+                                 h_norm, h_group));
+}
+
+int pasa_select(void* stream, const void* qc, const void* kc, const float* h_norm, const float* noise, int64_t BH,
+                int64_t NT, int D, int dtype, float scale, int use_cov_bias, int64_t ns, int32_t* indices,
+                uint32_t* sel_mask) {
+  if (dtype != PASA_BF16 && dtype != PASA_F32) return PASA_ERR_DTYPE;
+  if (D != 64 && D != 128) return PASA_ERR_UNSUPPORTED;
+  if (BH < 1 || BH > 65535 || NT < 1) return PASA_ERR_SHAPE;
+  if (ns < 1 || ns > NT) return PASA_ERR_SHAPE;
+  if (!qc || !kc || !indices || (use_cov_bias && !h_norm)) return PASA_ERR_NULL;
+  if (!std::isfinite(scale)) return PASA_ERR_SHAPE;
+  int st = check_select_fit(D, NT, ns);
+  if (st) return st;
+  if ((st = check_device())) return st;
+  return cuda_status(launch_select(static_cast<cudaStream_t>(stream), dtype, D, qc, kc, h_norm,
+                                   use_cov_bias ? noise : nullptr, BH, NT, ns, scale, use_cov_bias, indices,
+                                   sel_mask));
+}
+
+int pasa_attn(void* stream, const void* q, const void* k, const void* v, const void* kc, const void* vc,
+              const void* h_group, const int32_t* indices, const uint32_t* sel_mask, int64_t BH, int64_t T, int D,
+              int dtype, float scale, int64_t ns, void* o, uint32_t* err_word, int kernel) {
+  int st = check_common(BH, T, D, dtype);
+  if (st) return st;
+  const int64_t NT = cdiv(T, kBlock), NG = cdiv(NT, kGroup);
+  if (ns < 1 || ns > NT) return PASA_ERR_SHAPE;
+  if (!q || !k || !v || !kc || !vc || !h_group || !sel_mask || !o) return PASA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(kc) || !aligned16(vc) ||
+      !aligned16(h_group) || !aligned16(o))
+    return PASA_ERR_ALIGN;
+  if (!std::isfinite(scale)) return PASA_ERR_SHAPE;
+  if (kernel == PASA_ATTN_AUTO) kernel = (dtype == PASA_BF16) ? PASA_ATTN_TCGEN05 : PASA_ATTN_SIMT;
+  if ((st = check_device())) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kernel == PASA_ATTN_TCGEN05) {
+    if (dtype != PASA_BF16) return PASA_ERR_DTYPE;
+    return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word));
+  }
+  if (kernel != PASA_ATTN_SIMT) return PASA_ERR_UNSUPPORTED;
+  if (!indices) return PASA_ERR_NULL;
+  if (NG > 64) return PASA_ERR_SHAPE;  // the CUDA-core kernel keeps one word per group in shared memory
+  return cuda_status(launch_attn_simt(s, dtype, D, q, k, v, kc, vc, h_group, indices, sel_mask, BH, T, ns, scale,
+                                      o));
+}
+
+int pasa_forward(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
+                 int dtype, double density, float scale, int use_cov_bias, const float* noise, void* workspace,
+                 size_t workspace_bytes, void* o, int kernel) {
+  if (B < 1 || H < 1) return PASA_ERR_SHAPE;
+  int st = check_common(B * H, T, D, dtype);
+  if (st) return st;
+  if (!std::isfinite(density)) return PASA_ERR_DENSITY;
+  if (!q || !k || !v || !o) return PASA_ERR_NULL;
+  const int64_t BH = B * H, NT = cdiv(T, kBlock);
+  const int64_t NS = top_k_of(density, NT);
+  const Layout L = make_layout(BH, T, D, esize_of(dtype), NS);
+  if (!workspace || workspace_bytes < L.total) return PASA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PASA_ERR_ALIGN;
+  if ((st = check_select_fit(D, NT, NS))) return st;
+  if ((st = check_device())) return st;
+  char* w = static_cast<char*>(workspace);
+  void* qc = w + L.off_qc;
+  void* kc = w + L.off_kc;
+  void* vc = w + L.off_vc;
+  float* hn = reinterpret_cast<float*>(w + L.off_hnorm);
+  void* hg = w + L.off_hgroup;
+  int32_t* idx = reinterpret_cast<int32_t*>(w + L.off_idx);
+  uint32_t* mask = reinterpret_cast<uint32_t*>(w + L.off_mask);
+  uint32_t* err = reinterpret_cast<uint32_t*>(w + L.off_err);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = pasa_prep(stream, q, k, v, B, H, T, D, dtype, kBlock, kGroup, qc, kc, vc, hn, hg))) return st;
+  if ((st = pasa_select(stream, qc, kc, hn, noise, BH, NT, D, dtype, scale, use_cov_bias, NS, idx, mask)))
+    return st;
+  if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
+  return pasa_attn(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel);
+}
+
+int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal, int64_t cfg, int64_t H,
+               int64_t T, int D, int dtype, int64_t context_length, int64_t num_frame, int64_t frame_size,
+               int inverse) {
+  if (dtype != PASA_BF16 && dtype != PASA_F32) return PASA_ERR_DTYPE;
+  if (D < 8 || (D * esize_of(dtype)) % 16 != 0) return PASA_ERR_UNSUPPORTED;
+  if (cfg < 1 || H < 1 || T < 1 || context_length < 0 || num_frame < 1 || frame_size < 1) return PASA_ERR_SHAPE;
+  if (context_length + num_frame * frame_size != T) return PASA_ERR_SHAPE;  // placement.py:128
+  if (!src || !dst || !head_is_temporal) return PASA_ERR_NULL;
+  if (!aligned16(src) || !aligned16(dst)) return PASA_ERR_ALIGN;
+  int st = check_device();
+  if (st) return st;
+  return cuda_status(launch_place(static_cast<cudaStream_t>(stream), src, dst, head_is_temporal, cfg, H, T, D,
+                                  esize_of(dtype), context_length, num_frame, frame_size, inverse));
+}
+
+}  // extern "C"

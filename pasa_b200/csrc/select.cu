@@ -1,0 +1,242 @@
+// Covariance-aware top-k block selection.
+//
+// Restates svg/kernels/triton/group_pisa_attention.py:365-375:
+//   score[i, j] = dtype(qc_i . dtype(kc_j * scale))            (bf16 einsum)
+//               + log(h_norm_j + 1e-6) [+ noise_j]              (fp32 bias)
+//   indices[i]  = topk(score[i], NS).indices, largest first
+// without materialising the NT x NT score matrix in HBM: a CTA scores
+// kRows query blocks of one head against all key blocks into shared
+// memory, then each warp selects its row's top NS with a 4-pass radix
+// select over order-preserving uint32 keys and places the winners by rank.
+// Equal scores are ordered by lower block index (torch leaves the order of
+// exact ties unspecified).  The same pass writes the row's selection bitmask
+// (one 32-bit word per group of 32 key blocks), which the attention kernels
+// use instead of the reference's NS-long membership loop (:223-226).
+#include "common.cuh"
+
+namespace pasa {
+
+constexpr int kRows = 8;        // query blocks per CTA (one per warp)
+constexpr int kChunk = 64;      // key blocks staged per pass
+constexpr int kSelThreads = 256;
+constexpr int kCompactMax = 1024;  // NS up to this sorts from a compact list
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+struct SelectDims {
+  int64_t NT, NG, NTP, NS;
+  int D;
+};
+
+// Dynamic shared memory: qrow[kRows][D] f32 | kch[kChunk][D+1] f32 |
+// keys[kRows][NT] u32 | hist[kRows][256] u32 | mask[kRows][NG] u32 |
+// compact[kRows][NS] u64 (when NS <= kCompactMax)
+template <typename T, int D>
+__global__ void __launch_bounds__(kSelThreads) select_kernel(
+    const T* __restrict__ qc, const T* __restrict__ kc, const float* __restrict__ h_norm,
+    const float* __restrict__ noise, SelectDims dm, float scale, int use_cov_bias,
+    int32_t* __restrict__ indices, uint32_t* __restrict__ sel_mask) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t NT = dm.NT, NG = dm.NG, NTP = dm.NTP, NS = dm.NS;
+  float* qrow = reinterpret_cast<float*>(smem_raw);
+  float* kch = qrow + kRows * D;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(kch + kChunk * (D + 1));
+  uint32_t* hist = keys + kRows * NT;
+  uint32_t* maskw = hist + kRows * 256;
+  uint64_t* compact = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(maskw + kRows * NG) + 7) & ~uintptr_t(7));
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t bh = blockIdx.y;
+  const int64_t i0 = int64_t(blockIdx.x) * kRows;
+  const int nrows = int((NT - i0 < kRows) ? (NT - i0) : int64_t(kRows));
+  const float scale32 = scale;
+
+  for (int x = tid; x < kRows * D; x += kSelThreads) {
+    const int r = x / D, c = x % D;
+    qrow[x] = (r < nrows) ? Elem<T>::load(qc + (bh * NTP + i0 + r) * D + c) : 0.f;
+  }
+
+  // ---- scores ---------------------------------------------------------
+  const int jl = tid % kChunk;          // key within chunk
+  const int rg = tid / kChunk;          // rows rg*2, rg*2+1
+  for (int64_t j0 = 0; j0 < NT; j0 += kChunk) {
+    __syncthreads();
+    for (int x = tid; x < kChunk * D; x += kSelThreads) {
+      const int jj = x / D, c = x % D;
+      float val = 0.f;
+      if (j0 + jj < NT) val = Elem<T>::round(Elem<T>::load(kc + (bh * NTP + j0 + jj) * D + c) * scale32);
+      kch[jj * (D + 1) + c] = val;
+    }
+    __syncthreads();
+    const int64_t j = j0 + jl;
+    if (j < NT) {
+      float bias = 0.f;
+      if (use_cov_bias) {
+        bias = logf(h_norm[bh * NT + j] + 1e-6f);
+        if (noise) bias = bias + noise[bh * NT + j];
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = rg * 2 + rr;
+        if (r < nrows) {
+          const float* qv = qrow + r * D;
+          const float* kv = kch + jl * (D + 1);
+          float dot = 0.f;
+#pragma unroll 16
+          for (int c = 0; c < D; ++c) dot = fmaf(qv[c], kv[c], dot);
+          float s = Elem<T>::round(dot);
+          if (use_cov_bias) s = s + bias;
+          keys[r * NT + j] = order_key(s);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- per-row radix select + rank placement (one warp per row) --------
+  if (warp >= nrows) return;
+  const int64_t row = i0 + warp;
+  const uint32_t* rk = keys + warp * NT;
+  uint32_t* h = hist + warp * 256;
+  uint32_t* mw = maskw + warp * NG;
+
+  uint32_t prefix = 0, pmask = 0;
+  uint32_t remaining = uint32_t(NS);
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = lane; b < 256; b += 32) h[b] = 0;
+    __syncwarp();
+    for (int64_t j = lane; j < NT; j += 32) {
+      const uint32_t kj = rk[j];
+      if ((kj & pmask) == prefix) atomicAdd(&h[(kj >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    // lane owns buckets 255-8*lane ... 248-8*lane (descending)
+    uint32_t cnt[8], tot = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) { cnt[u] = h[255 - 8 * lane - u]; tot += cnt[u]; }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    const uint32_t excl = incl - tot;
+    const uint32_t hit = __ballot_sync(0xffffffffu, incl >= remaining);
+    const int src = __ffs(hit) - 1;  // first lane whose range reaches `remaining`
+    uint32_t bucket = 0, above = 0;
+    if (lane == src) {
+      uint32_t c = excl;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (c + cnt[u] >= remaining) { bucket = 255 - 8 * lane - u; above = c; break; }
+        c += cnt[u];
+      }
+    }
+    bucket = __shfl_sync(0xffffffffu, bucket, src);
+    above = __shfl_sync(0xffffffffu, above, src);
+    remaining -= above;
+    prefix |= bucket << shift;
+    pmask |= 0xFFu << shift;
+    __syncwarp();
+  }
+  const uint32_t kth = prefix;  // key of the NS-th largest score
+  // ties at kth: take the `remaining` lowest block indices
+  for (int64_t w = lane; w < NG; w += 32) mw[w] = 0;
+  __syncwarp();
+  uint32_t taken = 0;
+  for (int64_t j0 = 0; j0 < NT; j0 += 32) {
+    const int64_t j = j0 + lane;
+    const uint32_t kj = (j < NT) ? rk[j] : 0u;
+    const bool eq = (j < NT) && (kj == kth);
+    const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
+    const uint32_t rank_eq = taken + __popc(eqb & ((1u << lane) - 1u));
+    const bool sel = (j < NT) && (kj > kth || (eq && rank_eq < remaining));
+    const uint32_t selb = __ballot_sync(0xffffffffu, sel);
+    taken += __popc(eqb);
+    if (lane == 0) mw[j0 >> 5] = selb;  // j0 is a multiple of 32: one word per step
+  }
+  __syncwarp();
+
+  int32_t* out = indices + (bh * NT + row) * NS;
+  if (NS <= kCompactMax) {
+    // compact (key, index) of the selected blocks, then place by rank
+    uint64_t* cl = compact + int64_t(warp) * NS;
+    uint32_t base = 0;
+    for (int64_t j0 = 0; j0 < NT; j0 += 32) {
+      const int64_t j = j0 + lane;
+      const bool sel = (mw[j0 >> 5] >> lane) & 1u;
+      const uint32_t b = __ballot_sync(0xffffffffu, sel);
+      if (sel) {
+        const uint32_t pos = base + __popc(b & ((1u << lane) - 1u));
+        // larger composite = better: key, then lower index
+        cl[pos] = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
+      }
+      base += __popc(b);
+    }
+    __syncwarp();
+    for (int64_t e = lane; e < NS; e += 32) {
+      const uint64_t me = cl[e];
+      int64_t rank = 0;
+      for (int64_t f = 0; f < NS; ++f) rank += (cl[f] > me) ? 1 : 0;
+      out[rank] = int32_t(0xFFFFFFFFu - uint32_t(me & 0xFFFFFFFFu));
+    }
+  } else {
+    for (int64_t j = lane; j < NT; j += 32) {
+      if (!((mw[j >> 5] >> (j & 31)) & 1u)) continue;
+      const uint64_t me = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
+      int64_t rank = 0;
+      for (int64_t f = 0; f < NT; ++f) {
+        if (!((mw[f >> 5] >> (f & 31)) & 1u)) continue;
+        const uint64_t o = (uint64_t(rk[f]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(f));
+        rank += (o > me) ? 1 : 0;
+      }
+      out[rank] = int32_t(j);
+    }
+  }
+  if (sel_mask) {
+    uint32_t* mo = sel_mask + (bh * NT + row) * NG;
+    for (int64_t w = lane; w < NG; w += 32) mo[w] = mw[w];
+  }
+}
+
+size_t select_smem_bytes(int D, int64_t NT, int64_t NG, int64_t NS) {
+  size_t b = sizeof(float) * (kRows * D + kChunk * (D + 1));
+  b += sizeof(uint32_t) * (kRows * NT + kRows * 256 + kRows * NG);
+  b = (b + 7) & ~size_t(7);
+  if (NS <= kCompactMax) b += sizeof(uint64_t) * kRows * NS;
+  return b;
+}
+
+template <typename T, int D>
+static cudaError_t launch_select_t(cudaStream_t st, const void* qc, const void* kc, const float* hn,
+                                   const float* noise, int64_t BH, SelectDims dm, float scale,
+                                   int use_cov_bias, int32_t* idx, uint32_t* mask) {
+  const size_t smem = select_smem_bytes(D, dm.NT, dm.NG, dm.NS);
+  auto kern = select_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid{unsigned(cdiv(dm.NT, kRows)), unsigned(BH), 1u};
+  kern<<<grid, kSelThreads, smem, st>>>(static_cast<const T*>(qc), static_cast<const T*>(kc), hn, noise, dm,
+                                        scale, use_cov_bias, idx, mask);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select(cudaStream_t st, int dtype, int D, const void* qc, const void* kc,
+                          const float* hn, const float* noise, int64_t BH, int64_t NT, int64_t NS,
+                          float scale, int use_cov_bias, int32_t* idx, uint32_t* mask) {
+  SelectDims dm;
+  dm.NT = NT; dm.NG = cdiv(NT, kGroup); dm.NTP = dm.NG * kGroup; dm.NS = NS; dm.D = D;
+  if (dtype == PASA_BF16) {
+    if (D == 64) return launch_select_t<__nv_bfloat16, 64>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+    return launch_select_t<__nv_bfloat16, 128>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+  }
+  if (D == 64) return launch_select_t<float, 64>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+  return launch_select_t<float, 128>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+}
+
+}  // namespace pasa

@@ -1,0 +1,233 @@
+"""Host-side mirror of the reference's PASA operator interface.
+
+``pisa_pg_attention`` keeps the signature, argument meaning and error
+behaviour of ZHANGWENTAI/PASA ``svg/kernels/triton/group_pisa_attention.py:
+307-398`` and runs on the B200 through the C ABI of ``libpasa_b200.so``
+(``include/pasa_b200.h``).  PyTorch only provides device memory, the current
+stream and the random draw of ``use_random``; there is no CPU or Triton path.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"pasa_b200 supports bfloat16 and float32 inputs, got {t.dtype}") from None
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be [B, H, T, D], got shape {tuple(t.shape)}")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (pasa_b200 has no CPU path)")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError(f"q, k, v must share one shape, got {tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share one dtype")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, v must be on one device")
+    _dtype_code(q)
+
+
+class Stages:
+    """Intermediates of one call, allocated by torch (used for verbose output
+    and parity tests)."""
+
+    def __init__(self, B, H, T, D, NT, NG, NS, dtype, device):
+        NTP = NG * 32
+        self.qc = torch.empty(B * H, NTP, D, dtype=dtype, device=device)
+        self.kc = torch.empty_like(self.qc)
+        self.vc = torch.empty_like(self.qc)
+        self.h_norm = torch.empty(B * H, NT, dtype=torch.float32, device=device)
+        self.h_group = torch.empty(B * H, NG, D, D, dtype=dtype, device=device)
+        self.indices = torch.empty(B * H, NT, NS, dtype=torch.int32, device=device)
+        self.sel_mask = torch.empty(B * H, NT, NG, dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.NT, self.NG, self.NS = NT, NG, NS
+
+
+def prep(q, k, v, st: Stages):
+    B, H, T, D = q.shape
+    lib = _lib.load()
+    _lib.check("pasa_prep", lib.pasa_prep(_stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, T,
+                                          D, _dtype_code(q), 64, 32, st.qc.data_ptr(), st.kc.data_ptr(),
+                                          st.vc.data_ptr(), st.h_norm.data_ptr(), st.h_group.data_ptr()))
+
+
+def select(st: Stages, D: int, dtype_code: int, scale: float, use_cov_bias: bool, noise=None,
+           device=None, qc=None, kc=None, h_norm=None):
+    lib = _lib.load()
+    qc = st.qc if qc is None else qc
+    kc = st.kc if kc is None else kc
+    h_norm = st.h_norm if h_norm is None else h_norm
+    _lib.check("pasa_select", lib.pasa_select(_stream_ptr(device or qc.device), qc.data_ptr(), kc.data_ptr(),
+                                              h_norm.data_ptr(), _ptr(noise), st.indices.shape[0], st.NT, D,
+                                              dtype_code, float(scale), int(bool(use_cov_bias)), st.NS,
+                                              st.indices.data_ptr(), st.sel_mask.data_ptr()))
+
+
+def attn(q, k, v, st: Stages, scale: float, o: torch.Tensor, kernel: int = _lib.ATTN_AUTO,
+         kc=None, vc=None, h_group=None, indices=None, sel_mask=None):
+    B, H, T, D = q.shape
+    lib = _lib.load()
+    kc = st.kc if kc is None else kc
+    vc = st.vc if vc is None else vc
+    h_group = st.h_group if h_group is None else h_group
+    indices = st.indices if indices is None else indices
+    sel_mask = st.sel_mask if sel_mask is None else sel_mask
+    _lib.check("pasa_attn", lib.pasa_attn(_stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                          kc.data_ptr(), vc.data_ptr(), h_group.data_ptr(), indices.data_ptr(),
+                                          sel_mask.data_ptr(), B * H, T, D, _dtype_code(q), float(scale), st.NS,
+                                          o.data_ptr(), st.err.data_ptr(), int(kernel)))
+
+
+def check_device_errors(st: Stages) -> None:
+    """Raise if a kernel reported a bounded-wait timeout (synchronises)."""
+    flags = int(st.err.item())
+    if flags & _lib.DEVERR_WAIT_TIMEOUT:
+        raise RuntimeError("pasa_b200: a device-side barrier wait timed out (error word %#x)" % flags)
+
+
+def run_stages(q, k, v, density=0.15, scale=None, use_cov_bias=True, noise=None, kernel=_lib.ATTN_AUTO):
+    """The op as three separate C-ABI calls; returns (o, Stages)."""
+    _check_qkv(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, T, D = q.shape
+    scale = D ** -0.5 if scale is None else scale
+    NT, NG, NS = _lib.derive(T, density)
+    with torch.cuda.device(q.device):
+        st = Stages(B, H, T, D, NT, NG, NS, q.dtype, q.device)
+        prep(q, k, v, st)
+        select(st, D, _dtype_code(q), scale, use_cov_bias, noise)
+        o = torch.empty_like(v)
+        attn(q, k, v, st, scale, o, kernel)
+    return o, st
+
+
+def pisa_pg_attention(
+    q, k, v,
+    density=0.15,
+    timestep=0,
+    block_size=64,
+    group_size=32,
+    scale=None,
+    use_cov_bias=True,
+    use_random=False,
+    verbose=False,
+    prompt_token_length: Optional[int] = None,
+    *,
+    kernel: int = _lib.ATTN_AUTO,
+):
+    """PASA forward: exact attention on the covariance-aware top-k blocks,
+    zero-order + per-group first-order correction on the rest.
+
+    Same arguments as the reference (group_pisa_attention.py:307-318):
+    q, k, v [B, H, T, D] CUDA tensors (bf16 or fp32); ``density`` is the
+    fraction of 64-token blocks attended exactly; ``scale`` defaults to
+    D**-0.5; ``use_cov_bias`` adds log(h_norm + 1e-6) to the block score;
+    ``use_random`` adds ``torch.randn_like`` noise to that bias (drawn here,
+    on the current CUDA generator, exactly as the reference draws it).
+    ``timestep`` and ``prompt_token_length`` are accepted and unused, as in
+    the reference.  Returns a new tensor like ``v``.
+    """
+    del timestep, prompt_token_length  # unused by the reference as well
+    if block_size != 64 or group_size != 32:
+        raise ValueError("pasa_b200 supports block_size=64 and group_size=32 (the reference's defaults)")
+    _check_qkv(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, T, K = q.shape
+    scale = K ** -0.5 if scale is None else scale
+    NT, NG, NS = _lib.derive(T, density, block_size, group_size)
+    noise = None
+    if use_cov_bias and use_random:
+        # torch.randn_like(log_bias), log_bias: [B, H, NT] fp32 (:368-370)
+        noise = torch.randn((B, H, NT), dtype=torch.float32, device=q.device)
+
+    if verbose:
+        o, st = run_stages(q, k, v, density, scale, use_cov_bias, noise, kernel)
+        hn = st.h_norm
+        print(f"NT={NT}, N_GROUPS={NG}, GROUP_SIZE={group_size}")
+        print(f"h_norm: mean={hn.mean():.2f}, max={hn.max():.2f}")
+        print(f"h_group: {tuple(st.h_group.shape)}")
+        print(f"top_k={NS}, density={density}")
+        return o
+
+    dcode = _dtype_code(q)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        ws_bytes = _lib.workspace_size(B, H, T, K, dcode, NS, block_size, group_size)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+        o = torch.empty_like(v)
+        _lib.check("pasa_forward", lib.pasa_forward(
+            _stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, T, K, dcode, float(density),
+            float(scale), int(bool(use_cov_bias)), _ptr(noise), ws.data_ptr(), ws_bytes, o.data_ptr(),
+            int(kernel)))
+    return o
+
+
+def piecewise_sparse_attention(q, k, v, density=0.15, block_size=64, use_random=False, **kwargs):
+    """The name the model processors call (svg/models/wan/attention.py:384,
+    svg/models/hyvideo/attention.py:640, :682); its source is not in the
+    reference tree, and the processors pass the arguments of
+    ``pisa_pg_attention``, so it is the same op."""
+    return pisa_pg_attention(q, k, v, density=density, block_size=block_size, use_random=use_random, **kwargs)
+
+
+# ---------------------------------------------------------------------------
+# token-layout permutation (svg/models/hyvideo/placement.py)
+# ---------------------------------------------------------------------------
+def _place(src, dst, best_mask_idx, context_length, num_frame, frame_size, inverse):
+    if src.dim() != 4 or dst.shape != src.shape:
+        raise ValueError("placement expects [cfg, H, T, D] tensors of one shape")
+    if not (src.is_cuda and dst.is_cuda):
+        raise ValueError("placement tensors must be CUDA tensors")
+    if not (src.is_contiguous() and dst.is_contiguous()):
+        raise ValueError("placement tensors must be contiguous")
+    cfg, H, T, D = src.shape
+    if T != context_length + num_frame * frame_size:  # placement.py:128, :366
+        raise AssertionError("seq_len must equal context_length + num_frame * frame_size")
+    idx = best_mask_idx.to(device=src.device, dtype=torch.int32).contiguous()
+    if idx.shape != (cfg, H):
+        raise ValueError(f"best_mask_idx must be [cfg, H] = {(cfg, H)}, got {tuple(idx.shape)}")
+    lib = _lib.load()
+    with torch.cuda.device(src.device):
+        _lib.check("pasa_place", lib.pasa_place(_stream_ptr(src.device), src.data_ptr(), dst.data_ptr(),
+                                                idx.data_ptr(), cfg, H, T, D, _dtype_code(src),
+                                                int(context_length), int(num_frame), int(frame_size),
+                                                int(inverse)))
+
+
+def hunyuan_sparse_head_placement(query, key, value, query_out, key_out, value_out, best_mask_idx,
+                                  context_length, num_frame, frame_size):
+    """Frame-major -> token-major for temporal heads (best_mask_idx == 1),
+    copy for spatial heads; writes the caller's outputs
+    (placement.py:124-153)."""
+    for src, dst in ((query, query_out), (key, key_out), (value, value_out)):
+        _place(src, dst, best_mask_idx, context_length, num_frame, frame_size, inverse=0)
+
+
+def hunyuan_hidden_states_placement(hidden_states, hidden_states_out, best_mask_idx, context_length, num_frame,
+                                    frame_size):
+    """Token-major -> frame-major for temporal heads (placement.py:360-387)."""
+    _place(hidden_states, hidden_states_out, best_mask_idx, context_length, num_frame, frame_size, inverse=1)
+    return hidden_states_out
