@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tcgen05", "simt"])
+    ap.add_argument("--heads", type=int, default=0, help="run only this many heads (small profiling cases)")
     return ap.parse_args()
 
 
@@ -234,6 +235,10 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     w = synth.WORKLOADS[args.config]
+    if args.heads:
+        import dataclasses
+
+        w = dataclasses.replace(w, heads=args.heads)
     heads = synth.shard_heads(w.heads, rank, world)
     nh = len(heads)
     kernel = {"auto": _lib.ATTN_AUTO, "tcgen05": _lib.ATTN_TCGEN05, "simt": _lib.ATTN_SIMT}[args.kernel]
