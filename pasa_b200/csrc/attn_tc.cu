@@ -18,7 +18,9 @@
 //     half's own selection bits.
 //   * warp 0: TMA producer (Q once, then K/V blocks or kc/vc/H_g of a group
 //     per step through a ring of stages); warp 1: TMEM owner and MMA issuer
-//     (one thread); warps 2-5: softmax, one thread per query row (TMEM lane).
+//     (one thread); warps 2-9: softmax, two threads per query row (TMEM
+//     lane), each owning half of the row's columns; the two partner warps
+//     exchange row maxima and probability sums through shared memory.
 //   * TMEM: O accumulator (D cols), two S/P buffers (64 cols; P is written
 //     back as packed bf16 over S), two U buffers (D/2 cols).  The first-order
 //     term is an MMA: U = bf16(w_t * q_t) (A operand from TMEM, w_t = scale *
@@ -38,12 +40,12 @@ namespace pasa {
 
 namespace tc {
 
-constexpr int kThreads = 192;          // 6 warps
+constexpr int kThreads = 320;          // 10 warps: TMA, MMA, 8 softmax
 constexpr int kRowsPerTile = 128;      // two query blocks
 constexpr float kRescaleThresh = 8.0f; // log2 units
 constexpr int kMaxNT = 4096;           // union list capacity (entries)
 constexpr int kMaxNG = kMaxNT / kGroup;
-constexpr uint64_t kPollLimit = 2000000000ull;  // ns a barrier wait may take before giving up
+constexpr uint64_t kPollLimit = kWaitLimitCycles;  // SM cycles a barrier wait may take before giving up
 
 template <int D>
 struct Cfg {
@@ -52,24 +54,35 @@ struct Cfg {
   static constexpr int kKVBytes = kBlock * D * 2;       // one K (or V) block
   static constexpr int kCBytes = kGroup * D * 2;        // kc (or vc) rows of one group
   static constexpr int kHBytes = D * D * 2;
-  static constexpr int kStageBytes = (2 * kKVBytes > 2 * kCBytes + kHBytes) ? 2 * kKVBytes : 2 * kCBytes + kHBytes;
-  static constexpr int kStages = (D == 128) ? 3 : 6;
-  static constexpr uint32_t kTxP1 = 2 * kKVBytes;
-  static constexpr uint32_t kTxP2 = 2 * kCBytes + kHBytes;
-  // TMEM columns
+  // one shared-memory region holds two rings, used one after the other:
+  // ring 1 (phase 1) slots hold K and V of a block, ring 2 (phase 2) slots
+  // hold kc, vc rows and H of a group
+  static constexpr int kSlot1 = 2 * kKVBytes;
+  static constexpr int kSlot2 = 2 * kCBytes + kHBytes;
+  static constexpr int kRingBytes = (D == 128) ? 5 * kSlot1 : 8 * kSlot1;
+  static constexpr int kS1 = kRingBytes / kSlot1;
+  static constexpr int kS2 = kRingBytes / kSlot2;
+  static constexpr uint32_t kTxP1 = kSlot1;
+  static constexpr uint32_t kTxP2 = kSlot2;
+  // TMEM columns: O (fp32), Q (packed bf16, the A operand of every score
+  // MMA), three S/P buffers, two U buffers
   static constexpr uint32_t kColO = 0;
-  static constexpr uint32_t kColS0 = 128;
-  static constexpr uint32_t kColU0 = 256;
+  static constexpr uint32_t kColQ = 128;
+  static constexpr uint32_t kColS0 = 192;
+  static constexpr uint32_t kColU0 = 384;
   static constexpr uint32_t kTmemCols = 512;
   // shared memory carve-up (offsets from a 1024-aligned base)
   static constexpr int kOffQ = 0;
-  static constexpr int kOffStages = kQBytes;
-  static constexpr int kOffUnion = kOffStages + kStages * kStageBytes;
-  static constexpr int kOffMask = kOffUnion + kMaxNT * 4;
-  static constexpr int kOffBar = kOffMask + 2 * kMaxNG * 4;
-  static constexpr int kNumBars = 2 * kStages + 1 + 2 + 2 + 2;
+  static constexpr int kOffRing = kQBytes;
+  static constexpr int kOffUnion = kOffRing + kRingBytes;             // u16 [kMaxNT]
+  static constexpr int kOffMask = kOffUnion + kMaxNT * 2;              // u32 [2][kMaxNG]
+  static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][2 halves][128]
+  static constexpr int kOffBar = kOffXch + 2 * 2 * kRowsPerTile * 4;
+  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 1 + 1 + 3 + 3 + 2;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
+  static_assert(kS1 >= 3 && kS2 >= 2, "ring too small");
+  static_assert(kColU0 + 2 * 64 <= kTmemCols, "TMEM budget");
 };
 
 struct Maps {
@@ -84,6 +97,23 @@ struct Params {
   uint32_t* err;
 };
 
+// Optional step tracer (compile with -DPASA_TRACE): the CTA at grid (0, 0)
+// records SM clock stamps of its pipeline events for the first kTraceSteps
+// steps into g_pasa_trace[event][step]: 0 producer issue, 1 S issue, 2 P.V
+// issue, 4+w softmax warp w sees S, 12+w softmax warp w done;
+// pasa_trace_read() copies them out.
+#ifdef PASA_TRACE
+constexpr int kTraceSteps = 1024;
+__device__ unsigned long long g_pasa_trace[24][kTraceSteps];
+#define PASA_TRACE_MARK(ev, step)                                                        \
+  do {                                                                                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (step) < kTraceSteps)                       \
+      g_pasa_trace[(ev)][(step)] = clock64();                                             \
+  } while (0)
+#else
+#define PASA_TRACE_MARK(ev, step) do { } while (0)
+#endif
+
 __device__ __forceinline__ void report(uint32_t* err) {
   if (err) atomicOr(err, PASA_DEVERR_WAIT_TIMEOUT);
 }
@@ -93,16 +123,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   using C = Cfg<D>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint32_t* ulist = reinterpret_cast<uint32_t*>(sm + C::kOffUnion);
+  uint16_t* ulist = reinterpret_cast<uint16_t*>(sm + C::kOffUnion);  // (block << 2) | half bits
   uint32_t* maskw = reinterpret_cast<uint32_t*>(sm + C::kOffMask);  // [2][kMaxNG]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + C::kStages;
-  uint64_t* q_full = bars + 2 * C::kStages;
-  uint64_t* s_full = q_full + 1;   // [2]
-  uint64_t* p_ready = s_full + 2;  // [2]
-  uint64_t* o_done = p_ready + 2;  // [2]
+  uint64_t* full1 = bars;
+  uint64_t* empty1 = full1 + C::kS1;
+  uint64_t* full2 = empty1 + C::kS1;
+  uint64_t* empty2 = full2 + C::kS2;
+  uint64_t* q_full = empty2 + C::kS2;
+  uint64_t* q_tmem = q_full + 1;   // Q copied into TMEM by the softmax warps
+  uint64_t* s_full = q_tmem + 1;   // [3]
+  uint64_t* p_ready = s_full + 3;  // [3]
+  uint64_t* o_done = p_ready + 3;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffSlot);
+  float* xch = reinterpret_cast<float*>(sm + C::kOffXch);
   __shared__ uint32_t s_nu;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -113,9 +147,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 
   // ---- set-up: barriers, TMEM, selection bits, union list -------------
   if (tid == 0) {
-    for (int s = 0; s < C::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < C::kS1; ++s) { mbar_init(&full1[s], 1); mbar_init(&empty1[s], 1); }
+    for (int s = 0; s < C::kS2; ++s) { mbar_init(&full2[s], 1); mbar_init(&empty2[s], 1); }
     mbar_init(q_full, 1);
-    for (int b = 0; b < 2; ++b) { mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], 4); mbar_init(&o_done[b], 1); }
+    mbar_init(q_tmem, 8);
+    for (int b = 0; b < 3; ++b) { mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], 8); }
+    for (int b = 0; b < 2; ++b) mbar_init(&o_done[b], 1);
     fence_barrier_init();
   }
   if (warp == 1) { tmem_alloc(tmem_slot, C::kTmemCols); tmem_relinquish(); }
@@ -147,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         const int b = __ffs(rem) - 1;
         rem &= rem - 1;
         const uint32_t j = uint32_t(w * 32 + b);
-        ulist[pos++] = (j << 2) | ((ma >> b) & 1u) | (((mb >> b) & 1u) << 1);
+        ulist[pos++] = uint16_t((j << 2) | ((ma >> b) & 1u) | (((mb >> b) & 1u) << 1));
       }
       base += __shfl_sync(0xffffffffu, incl, 31);
     }
@@ -162,6 +199,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 
   if (warp == 0) {
     // ================= TMA producer =================
+#ifdef PASA_TRACE
+    if (lane == 1 && blockIdx.x == 0 && blockIdx.y == 0) {  // trace only: stamp data arrival (event 3)
+      for (int64_t n = 0; n < nU && n < kTraceSteps; ++n)
+        if (mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)) PASA_TRACE_MARK(3, n);
+    }
+#endif
     if (lane == 0) {
       bool ok = true;
       int64_t issued = 0;
@@ -169,61 +212,104 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       mbar_arrive_expect_tx(q_full, C::kQBytes);
       for (int bx = 0; bx < C::kBoxes; ++bx)
         tma_load_3d(sm + C::kOffQ + bx * (kRowsPerTile * 128), &maps.q, q_full, bx * 64, row0, int32_t(bh));
-      for (int64_t n = 0; n < total && ok; ++n) {
-        const int s = int(n % C::kStages);
-        const uint32_t ph = uint32_t((n / C::kStages) & 1);
-        if (!mbar_wait_bounded(&empty[s], ph ^ 1u, kPollLimit)) { ok = false; break; }
-        unsigned char* st = sm + C::kOffStages + s * C::kStageBytes;
-        if (n < nU) {
-          const int32_t j = int32_t(ulist[n] >> 2);
-          mbar_arrive_expect_tx(&full[s], C::kTxP1);
-          for (int bx = 0; bx < C::kBoxes; ++bx) {
-            tma_load_3d(st + bx * (kBlock * 128), &maps.k, &full[s], bx * 64, j * kBlock, int32_t(bh));
-            tma_load_3d(st + C::kKVBytes + bx * (kBlock * 128), &maps.v, &full[s], bx * 64, j * kBlock, int32_t(bh));
-          }
-        } else {
-          const int32_t g = int32_t(n - nU);
-          mbar_arrive_expect_tx(&full[s], C::kTxP2);
-          for (int bx = 0; bx < C::kBoxes; ++bx) {
-            tma_load_3d(st + bx * (kGroup * 128), &maps.kc, &full[s], bx * 64, g * kGroup, int32_t(bh));
-            tma_load_3d(st + C::kCBytes + bx * (kGroup * 128), &maps.vc, &full[s], bx * 64, g * kGroup, int32_t(bh));
-            tma_load_3d(st + 2 * C::kCBytes + bx * (D * 128), &maps.h, &full[s], bx * 64, 0,
-                        int32_t(bh * NG + g));
-          }
+      // Phase 1: K and V of every union block through ring 1
+      for (int64_t n = 0; n < nU && ok; ++n) {
+        const int s = int(n % C::kS1);
+        if (!mbar_wait_bounded(&empty1[s], uint32_t((n / C::kS1) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
+        PASA_TRACE_MARK(0, n);
+        unsigned char* st = sm + C::kOffRing + s * C::kSlot1;
+        const int32_t j = int32_t(ulist[n] >> 2);
+        mbar_arrive_expect_tx(&full1[s], C::kTxP1);
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          tma_load_3d(st + bx * (kBlock * 128), &maps.k, &full1[s], bx * 64, j * kBlock, int32_t(bh));
+          tma_load_3d(st + C::kKVBytes + bx * (kBlock * 128), &maps.v, &full1[s], bx * 64, j * kBlock,
+                      int32_t(bh));
         }
         issued = n + 1;
       }
+      // ring 2 aliases ring 1: every phase-1 slot must be released first
+      for (int64_t n = (nU > C::kS1 ? nU - C::kS1 : 0); n < nU && ok; ++n)
+        if (!mbar_wait_bounded(&empty1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)) ok = false;
+      // Phase 2: kc, vc rows and H of every group through ring 2
+      for (int64_t g = 0; g < NG && ok; ++g) {
+        const int s = int(g % C::kS2);
+        if (!mbar_wait_bounded(&empty2[s], uint32_t((g / C::kS2) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
+        PASA_TRACE_MARK(0, nU + g);
+        unsigned char* st = sm + C::kOffRing + s * C::kSlot2;
+        mbar_arrive_expect_tx(&full2[s], C::kTxP2);
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          tma_load_3d(st + bx * (kGroup * 128), &maps.kc, &full2[s], bx * 64, int32_t(g * kGroup), int32_t(bh));
+          tma_load_3d(st + C::kCBytes + bx * (kGroup * 128), &maps.vc, &full2[s], bx * 64, int32_t(g * kGroup),
+                      int32_t(bh));
+          tma_load_3d(st + 2 * C::kCBytes + bx * (D * 128), &maps.h, &full2[s], bx * 64, 0, int32_t(bh * NG + g));
+        }
+        issued = nU + g + 1;
+      }
       if (!ok) report(P.err);
       // drain: let this thread's last copies land before the CTA can exit
-      const int64_t first = issued > C::kStages ? issued - C::kStages : 0;
-      for (int64_t n = first; n < issued; ++n) {
-        const int s = int(n % C::kStages);
-        mbar_wait_bounded(&full[s], uint32_t((n / C::kStages) & 1), kPollLimit);
+      for (int64_t n = (issued > 3 ? issued - 3 : 0); n < issued; ++n) {
+        if (n < nU) mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit);
+        else mbar_wait_bounded(&full2[(n - nU) % C::kS2], uint32_t(((n - nU) / C::kS2) & 1), kPollLimit);
       }
     }
   } else if (warp == 1) {
     // ================= MMA issuer =================
+    // S of step n+2 is issued before P.V of step n, so the softmax never
+    // waits for its scores; S/P and U buffers rotate over three slots.
     if (lane == 0) {
       constexpr uint32_t idS64 = umma_idesc_bf16(128, 64, false, false);
       constexpr uint32_t idS32 = umma_idesc_bf16(128, 32, false, false);
       constexpr uint32_t idPV = umma_idesc_bf16(128, D, false, true);
-      const uint32_t qaddr = smem_u32(sm + C::kOffQ);
-      bool ok = mbar_wait_bounded(q_full, 0, kPollLimit);
+      bool ok = mbar_wait_bounded(q_tmem, 0, kPollLimit);
+      tc_fence_after();
 
-      auto issue_pv = [&](int64_t m) -> bool {
-        const int b = int(m & 1);
-        if (!mbar_wait_bounded(&p_ready[b], uint32_t((m >> 1) & 1), kPollLimit)) return false;
+      auto slot_addr = [&](int64_t n) -> uint32_t {
+        return (n < nU) ? smem_u32(sm + C::kOffRing + int(n % C::kS1) * C::kSlot1)
+                        : smem_u32(sm + C::kOffRing + int((n - nU) % C::kS2) * C::kSlot2);
+      };
+      // Event loop: issue whichever of the next S (scores, needs its TMA
+      // data) or the next P.V (needs the softmax) is ready, never blocking
+      // one on the other.  P.V completion releases ring slots, so P.V goes
+      // first when both are ready.  S runs at most two steps ahead of P.V
+      // (three S/P buffers).  Ring 2 reuses ring 1's memory, so group scores
+      // wait until every exact-block P.V is issued.
+      auto data_ready = [&](int64_t n) -> bool {
+        if (n < nU) return mbar_test(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1));
+        const int64_t g = n - nU;
+        return mbar_test(&full2[g % C::kS2], uint32_t((g / C::kS2) & 1));
+      };
+      auto issue_s = [&](int64_t n) {
+        PASA_TRACE_MARK(1, n);
         tc_fence_after();
-        const int s = int(m % C::kStages);
-        const uint32_t st = smem_u32(sm + C::kOffStages + s * C::kStageBytes);
+        const uint32_t st = slot_addr(n);
+        const int b = int(n % 3);
         const uint32_t tS = tmem + C::kColS0 + 64u * b;
-        const uint32_t tU = tmem + C::kColU0 + 64u * b;
+        const int rows = (n < nU) ? kBlock : kGroup;
+        const uint32_t id = (n < nU) ? idS64 : idS32;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int bx = kk / 4, ko = (kk % 4) * 32;
+          const uint64_t bd = umma_desc_sw128(st + bx * (rows * 128) + ko, 16, 1024);
+          mma_ts(tS, tmem + C::kColQ + kk * 8, bd, id, kk > 0 ? 1u : 0u);
+        }
+        PASA_TRACE_MARK(20, n);
+        tc_commit(&s_full[b]);
+        PASA_TRACE_MARK(21, n);
+      };
+      auto issue_pv = [&](int64_t m) {
+        const int b = int(m % 3);
+        PASA_TRACE_MARK(2, m);
+        tc_fence_after();
+        const uint32_t st = slot_addr(m);
+        const uint32_t tS = tmem + C::kColS0 + 64u * b;
+        const uint32_t tU = tmem + C::kColU0 + 64u * uint32_t(m & 1);
         if (m < nU) {
 #pragma unroll
           for (int kk = 0; kk < kBlock / 16; ++kk) {
             const uint64_t bd = umma_desc_sw128(st + C::kKVBytes + kk * 2048, C::kKVBytes / C::kBoxes, 1024);
             mma_ts(tmem + C::kColO, tS + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
           }
+          tc_commit(&empty1[m % C::kS1]);
         } else {
 #pragma unroll
           for (int kk = 0; kk < kGroup / 16; ++kk) {
@@ -235,57 +321,81 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             const uint64_t bd = umma_desc_sw128(st + 2 * C::kCBytes + kk * 2048, C::kHBytes / C::kBoxes, 1024);
             mma_ts(tmem + C::kColO, tU + kk * 8, bd, idPV, 1u);
           }
+          tc_commit(&empty2[(m - nU) % C::kS2]);
         }
-        tc_commit(&empty[s]);
-        tc_commit(&o_done[b]);
-        return true;
+        PASA_TRACE_MARK(22, m);
+        tc_commit(&o_done[m & 1]);
+        PASA_TRACE_MARK(23, m);
       };
 
-      for (int64_t n = 0; n < total && ok; ++n) {
-        const int s = int(n % C::kStages);
-        const uint32_t ph = uint32_t((n / C::kStages) & 1);
-        const int b = int(n & 1);
-        if (!mbar_wait_bounded(&full[s], ph, kPollLimit)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t st = smem_u32(sm + C::kOffStages + s * C::kStageBytes);
-        const uint32_t tS = tmem + C::kColS0 + 64u * b;
-        if (n < nU) {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int bx = kk / 4, ko = (kk % 4) * 32;
-            const uint64_t ad = umma_desc_sw128(qaddr + bx * (kRowsPerTile * 128) + ko, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(st + bx * (kBlock * 128) + ko, 16, 1024);
-            mma_ss(tS, ad, bd, idS64, kk > 0 ? 1u : 0u);
-          }
-        } else {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int bx = kk / 4, ko = (kk % 4) * 32;
-            const uint64_t ad = umma_desc_sw128(qaddr + bx * (kRowsPerTile * 128) + ko, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(st + bx * (kGroup * 128) + ko, 16, 1024);
-            mma_ss(tS, ad, bd, idS32, kk > 0 ? 1u : 0u);
-          }
+      int64_t ns = 0, npv = 0;
+      uint64_t idle_since = 0;
+      while (ok && npv < total) {
+        bool progressed = false;
+        if (npv < ns && mbar_test(&p_ready[npv % 3], uint32_t((npv / 3) & 1))) {
+          issue_pv(npv++);
+          progressed = true;
         }
-        tc_commit(&s_full[b]);
-        if (n >= 1 && !issue_pv(n - 1)) { ok = false; break; }
+        // phase 2 runs one step ahead only: its U buffers are double, not triple
+        if (ns < total && (ns < nU ? ns <= npv + 2 : (npv >= nU && ns <= npv + 1)) && data_ready(ns)) {
+          issue_s(ns++);
+          progressed = true;
+        }
+        if (progressed) {
+          idle_since = 0;
+        } else {
+          // back off: this warp shares its SM sub-partition with two softmax warps
+          __nanosleep(32);
+          if (idle_since == 0) idle_since = sm_cycles();
+          else if (sm_cycles() - idle_since > kPollLimit) ok = false;
+        }
       }
-      if (ok && total >= 1) ok = issue_pv(total - 1);
       if (!ok) report(P.err);
     }
     __syncwarp();
   } else {
-    // ================= softmax / correction (warps 2..5) =================
+    // ================= softmax / correction (warps 2..9) =================
+    // Two warps share each TMEM lane quadrant (one query row per lane); warp
+    // half `ch` owns half of the row's columns.  Partners exchange the row max
+    // (and, per group, the probability sum) through shared memory.
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
+    const int ch = (warp - 2) >> 2;            // column half of this warp
     const int r = quad * 32 + lane;            // tile row == TMEM lane
     const int half = r >> 6;                   // 0: block A, 1: block B
-    const bool live = (half == 0) || hasB;
+    const bool live = (half == 0) || hasB;     // uniform per warp
+    const int bar_id = 1 + quad;               // named barrier of the two partner warps
     const uint32_t lane_base = uint32_t(quad * 32) << 16;
     const float scale32 = P.scale;
     const float sm_scale = scale32 * kLog2e;
     const int64_t last_len = P.T - (NT - 1) * kBlock;
+    constexpr int DH = D / 2;                  // output columns per partner
     float m_true = -INFINITY, m_used = -INFINITY, l1 = 0.f, gl = 0.f;
-    uint32_t qpk[D / 2];  // this row of Q as packed bf16 pairs (phase 2)
+    uint32_t xslot = 0;
+    auto exchange = [&](float v) -> float {
+      xch[(xslot * 2 + ch) * kRowsPerTile + r] = v;
+      named_bar_sync(bar_id, 64);
+      const float o = xch[(xslot * 2 + (ch ^ 1)) * kRowsPerTile + r];
+      xslot ^= 1u;
+      return o;
+    };
+    uint32_t qpk[DH / 2];  // this row's half of Q as packed bf16 pairs
     bool ok = mbar_wait_bounded(q_full, 0, kPollLimit);
+    {  // copy this row's half of Q into TMEM, the A operand of the score MMAs
+#pragma unroll
+      for (int x = 0; x < DH / 8; ++x) {
+        const int d = ch * DH + x * 8, bx = d / 64, c = (d % 64) / 8;
+        const uint4 v = *reinterpret_cast<const uint4*>(sm + C::kOffQ + bx * (kRowsPerTile * 128) + r * 128 +
+                                                       ((c ^ (r & 7)) << 4));
+        qpk[x * 4 + 0] = v.x; qpk[x * 4 + 1] = v.y; qpk[x * 4 + 2] = v.z; qpk[x * 4 + 3] = v.w;
+      }
+#pragma unroll
+      for (int c0 = 0; c0 < DH / 2; c0 += 16)
+        tmem_st16(tmem + lane_base + C::kColQ + ch * (DH / 2) + c0, *reinterpret_cast<uint32_t(*)[16]>(&qpk[c0]));
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_tmem);
+    }
 
     auto rescale_o = [&](int64_t n, float alpha) -> bool {
       // O is consistent once the MMAs of step n-1 have completed
@@ -295,44 +405,43 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         tc_fence_after();
       }
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 16) {
+      for (int c0 = 0; c0 < DH; c0 += 16) {
         uint32_t v[16];
-        tmem_ld16(tmem + lane_base + C::kColO + c0, v);
+        tmem_ld16(tmem + lane_base + C::kColO + ch * DH + c0, v);
         tmem_wait_ld();
 #pragma unroll
         for (int x = 0; x < 16; ++x) v[x] = __float_as_uint(__uint_as_float(v[x]) * alpha);
-        tmem_st16(tmem + lane_base + C::kColO + c0, v);
+        tmem_st16(tmem + lane_base + C::kColO + ch * DH + c0, v);
       }
       tmem_wait_st();
       return true;
     };
 
     for (int64_t n = 0; n < total && ok; ++n) {
-      const int b = int(n & 1);
-      if (!mbar_wait_bounded(&s_full[b], uint32_t((n >> 1) & 1), kPollLimit)) { ok = false; break; }
+      const int b = int(n % 3);
+      if (!mbar_wait_bounded(&s_full[b], uint32_t((n / 3) & 1), kPollLimit)) { ok = false; break; }
+      if (lane == 0) PASA_TRACE_MARK(4 + (warp - 2), n);
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + C::kColS0 + 64u * b;
       if (n < nU) {
         // ---------------- Phase 1: exact block ----------------
-        const uint32_t e = ulist[n];
+        const uint32_t e = ulist[n];  // (block << 2) | bit per half
         const int64_t j = e >> 2;
-        const bool active = live && ((e >> half) & 1u);
-        uint32_t pk[32];
+        const bool active = live && ((e >> half) & 1u);  // uniform per warp
+        uint32_t pk[16];
         if (active) {
-          uint32_t sv[64];
-          tmem_ld16(tS + 0, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
-          tmem_ld16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
-          tmem_ld16(tS + 32, *reinterpret_cast<uint32_t(*)[16]>(&sv[32]));
-          tmem_ld16(tS + 48, *reinterpret_cast<uint32_t(*)[16]>(&sv[48]));
+          uint32_t sv[32];
+          tmem_ld16(tS + ch * 32 + 0, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
+          tmem_ld16(tS + ch * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
           tmem_wait_ld();
-          const int nvalid = (j == NT - 1) ? int(last_len) : kBlock;  // key rows >= T masked (:178)
-          float s[64];
-          float mx = -INFINITY;
+          if (j == NT - 1) {  // key rows >= T are masked (:178); only the last block has them
+            const int nvalid = int(last_len) - ch * 32;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            s[c] = (c < nvalid) ? __uint_as_float(sv[c]) * sm_scale : -INFINITY;
-            mx = fmaxf(mx, s[c]);
+            for (int c = 0; c < 32; ++c)
+              if (c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
           }
+          float mx = max_tree32(sv);
+          mx = fmaxf(mx, exchange(mx)) * sm_scale;  // max commutes with the positive scale
           m_true = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;
           const bool need = grow && (m_used != -INFINITY);
@@ -342,55 +451,32 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           }
           l1 *= alpha;
           if (grow) m_used = mx;
-          float sum = 0.f;
-#pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float p0 = fast_exp2(s[c] - m_used), p1 = fast_exp2(s[c + 1] - m_used);
-            sum += p0 + p1;
-            pk[c / 2] = pack_bf16x2(p0, p1);
-          }
-          l1 += sum;
+          l1 += exp2_pack32(sv, sm_scale, -m_used, pk);
         } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) pk[c] = 0u;
+          for (int c = 0; c < 16; ++c) pk[c] = 0u;
         }
-        tmem_st16(tS + 0, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-        tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+        tmem_st16(tS + ch * 16, pk);
         tmem_wait_st();
       } else {
         // ---------------- Phase 2: group g ----------------
         const int64_t g = n - nU;
-        if (g == 0) {  // this row of Q, read once from the swizzled tile
-          const unsigned char* qrow = sm + C::kOffQ;
-#pragma unroll
-          for (int bx = 0; bx < C::kBoxes; ++bx)
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const uint4 v = *reinterpret_cast<const uint4*>(qrow + bx * (kRowsPerTile * 128) + r * 128 +
-                                                             ((c ^ (r & 7)) << 4));
-              qpk[bx * 32 + c * 4 + 0] = v.x;
-              qpk[bx * 32 + c * 4 + 1] = v.y;
-              qpk[bx * 32 + c * 4 + 2] = v.z;
-              qpk[bx * 32 + c * 4 + 3] = v.w;
-            }
-        }
-        uint32_t pk[16];
-        uint32_t upk[D / 2];
+        uint32_t pk[8];
+        uint32_t upk[DH / 2];
         if (live) {
-          uint32_t sv[32];
-          tmem_ld16(tS + 0, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
-          tmem_ld16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
+          uint32_t sv[16];
+          tmem_ld16(tS + ch * 16, sv);
           tmem_wait_ld();
-          const uint32_t word = maskw[half * kMaxNG + g];
-          float a[32];
-          float mx = -INFINITY;
+          const uint32_t word = maskw[half * kMaxNG + g] >> (ch * 16);
+          const int64_t jb0 = g * kGroup + ch * 16;
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int64_t jb = g * kGroup + c;
-            const bool valid = (jb < NT) && !((word >> c) & 1u);  // :228
-            a[c] = valid ? __uint_as_float(sv[c]) * sm_scale : -INFINITY;
-            mx = fmaxf(mx, a[c]);
+          for (int c = 0; c < 16; ++c) {
+            const bool valid = (jb0 + c < NT) && !((word >> c) & 1u);  // :228
+            if (!valid) sv[c] = __float_as_uint(-INFINITY);
           }
+          float mx = max_tree16(sv);
+          mx = fmaxf(mx, exchange(mx));
+          mx = (mx == -INFINITY) ? mx : mx * sm_scale;
           const float m_true_new = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;  // m_used is finite for live rows here
           const float alpha = grow ? fast_exp2(m_used - mx) : 1.0f;
@@ -399,42 +485,48 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           }
           l1 *= alpha;
           if (grow) m_used = mx;
-          float psum = 0.f, wsum = 0.f;
+          float p[16];
+          const float negm = -m_used;
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const float p0 = fast_exp2(a[c] - m_used), p1 = fast_exp2(a[c + 1] - m_used);
-            const int64_t jb = g * kGroup + c;
-            const float len0 = (jb == NT - 1) ? float(last_len) : float(kBlock);
-            const float len1 = (jb + 1 == NT - 1) ? float(last_len) : float(kBlock);
-            psum += p0 + p1;
-            wsum += p0 * len0 + p1 * len1;
-            pk[c / 2] = pack_bf16x2(p0, p1);
+          for (int c = 0; c < 16; ++c) p[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
+          float psum = 0.f, wsum;
+          {
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 16; c += 2) { a0 += p[c]; a1 += p[c + 1]; }
+            psum = a0 + a1;
+            wsum = psum * float(kBlock);
+            if (jb0 <= NT - 1 && NT - 1 < jb0 + 16)  // the ragged last block has its own length (:220)
+              wsum += p[NT - 1 - jb0] * float(last_len - kBlock);
           }
+#pragma unroll
+          for (int c = 0; c < 16; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
+          psum += exchange(psum);
           // the reference's probabilities use the exact running max (:237, :243)
           gl += wsum * fast_exp2(m_used - m_true_new);
           m_true = m_true_new;
           const float w = psum * scale32;  // :253
 #pragma unroll
-          for (int x = 0; x < D / 2; ++x) {
-            __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(&qpk[x]);
-            const float2 qf = __bfloat1622float2(q2);
+          for (int x = 0; x < DH / 2; ++x) {
+            const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qpk[x]));
             upk[x] = pack_bf16x2(qf.x * w, qf.y * w);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) pk[c] = 0u;
+          for (int c = 0; c < 8; ++c) pk[c] = 0u;
 #pragma unroll
-          for (int x = 0; x < D / 2; ++x) upk[x] = 0u;
+          for (int x = 0; x < DH / 2; ++x) upk[x] = 0u;
         }
-        tmem_st16(tS + 0, pk);
-        const uint32_t tU = tmem + lane_base + C::kColU0 + 64u * b;
+        tmem_st8(tS + ch * 8, pk);
+        const uint32_t tU = tmem + lane_base + C::kColU0 + 64u * uint32_t(n & 1) + ch * (DH / 2);
 #pragma unroll
-        for (int c0 = 0; c0 < D / 2; c0 += 16)
+        for (int c0 = 0; c0 < DH / 2; c0 += 16)
           tmem_st16(tU + c0, *reinterpret_cast<uint32_t(*)[16]>(&upk[c0]));
         tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
+      if (lane == 0) PASA_TRACE_MARK(12 + (warp - 2), n);
       if (lane == 0) mbar_arrive(&p_ready[b]);
     }
 
@@ -446,24 +538,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     }
     const int64_t blk = (half == 0) ? blkA : blkB;
     const int64_t t = blk * kBlock + (r & 63);
-    if (__all_sync(0xffffffffu, ok) && live) {  // warp-uniform: tcgen05.ld is warp-collective
-      const bool store = t < P.T;
-      const float denom = l1 + gl * fast_exp2(m_true - m_used);
-      const float inv = 1.0f / denom;
-      __nv_bfloat16* orow = P.o + (bh * P.T + t) * D;
+    const bool wok = __all_sync(0xffffffffu, ok);
+    if (live) {
+      // partners combine their partial sums (both take part even after a failure)
+      const float l_tot = l1 + exchange(l1);
+      const float g_tot = gl + exchange(gl);
+      if (wok) {  // warp-uniform: tcgen05.ld is warp-collective
+        const bool store = t < P.T;
+        const float denom = l_tot + g_tot * fast_exp2(m_true - m_used);
+        const float inv = 1.0f / denom;
+        __nv_bfloat16* orow = P.o + (bh * P.T + t) * D + ch * DH;
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + lane_base + C::kColO + c0, v);
-        tmem_wait_ld();
-        uint4 out[2];
-        uint32_t* ow = reinterpret_cast<uint32_t*>(out);
+        for (int c0 = 0; c0 < DH; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_base + C::kColO + ch * DH + c0, v);
+          tmem_wait_ld();
+          uint4 out[2];
+          uint32_t* ow = reinterpret_cast<uint32_t*>(out);
 #pragma unroll
-        for (int x = 0; x < 8; ++x)
-          ow[x] = pack_bf16x2(__uint_as_float(v[2 * x]) * inv, __uint_as_float(v[2 * x + 1]) * inv);
-        if (store) {
-          reinterpret_cast<uint4*>(orow + c0)[0] = out[0];
-          reinterpret_cast<uint4*>(orow + c0)[1] = out[1];
+          for (int x = 0; x < 8; ++x)
+            ow[x] = pack_bf16x2(__uint_as_float(v[2 * x]) * inv, __uint_as_float(v[2 * x + 1]) * inv);
+          if (store) {
+            reinterpret_cast<uint4*>(orow + c0)[0] = out[0];
+            reinterpret_cast<uint4*>(orow + c0)[1] = out[1];
+          }
         }
       }
     }
@@ -538,3 +636,9 @@ cudaError_t launch_attn_tc(cudaStream_t st, int D, const void* q, const void* k,
 }
 
 }  // namespace pasa
+
+#ifdef PASA_TRACE
+extern "C" PASA_API int pasa_trace_read(void* host_dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(host_dst, pasa::tc::g_pasa_trace, bytes) == cudaSuccess ? 0 : PASA_ERR_CUDA;
+}
+#endif

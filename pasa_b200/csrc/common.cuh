@@ -36,7 +36,7 @@ template <> struct Elem<__nv_bfloat16> {
 // reference's tl.math.exp2 lowers to.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
-  asm volatile("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -109,22 +109,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-__device__ __forceinline__ uint64_t global_timer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
+// Non-blocking probe of a phase (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
 }
 
-// Bounded wait: returns false (the phase still incomplete) once `limit_ns`
-// nanoseconds have passed without the phase completing.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+// SM clock cycles (cheap to read; compared only within one thread).
+__device__ __forceinline__ uint64_t sm_cycles() { return clock64(); }
+
+// Bound on any single barrier wait: 4e9 SM cycles (about 2 s at B200 clocks,
+// against kernels of milliseconds).
+constexpr uint64_t kWaitLimitCycles = 4000000000ull;
+
+// Bounded wait: returns false (the phase still incomplete) once `limit`
+// SM cycles have passed without the phase completing.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = sm_cycles();
   for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > limit_ns) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    if (sm_cycles() - t0 > limit) return false;
   }
 }
 
@@ -222,6 +233,81 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, bool a_mn_m
        | ((b_mn_major ? 1u : 0u) << 16)
        | (uint32_t(N >> 3) << 17)
        | (uint32_t(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+
+// Named barrier over `nthreads` threads (multiple of 32); id 0 is __syncthreads.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Maximum of 32 / 16 fp32 values held as raw bits (shallow tree of 3-input max).
+__device__ __forceinline__ float max_tree32(const uint32_t (&v)[32]) {
+  float m[12];
+#pragma unroll
+  for (int i = 0; i < 10; ++i)
+    m[i] = fmax3(__uint_as_float(v[3 * i]), __uint_as_float(v[3 * i + 1]), __uint_as_float(v[3 * i + 2]));
+  m[10] = __uint_as_float(v[30]);
+  m[11] = __uint_as_float(v[31]);
+  const float a = fmax3(m[0], m[1], m[2]), b = fmax3(m[3], m[4], m[5]);
+  const float c = fmax3(m[6], m[7], m[8]), d = fmax3(m[9], m[10], m[11]);
+  return fmaxf(fmax3(a, b, c), d);
+}
+__device__ __forceinline__ float max_tree16(const uint32_t (&v)[16]) {
+  float m[6];
+#pragma unroll
+  for (int i = 0; i < 5; ++i)
+    m[i] = fmax3(__uint_as_float(v[3 * i]), __uint_as_float(v[3 * i + 1]), __uint_as_float(v[3 * i + 2]));
+  m[5] = __uint_as_float(v[15]);
+  return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]));
+}
+
+// Packed fp32 pair arithmetic (sm_100): d = a * b + c and d = a + b, lane-wise.
+__device__ __forceinline__ void fma_f32x2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                          float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add_f32x2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi);
+
+// p_c = 2^(s_c * scale + negm) for 32 raw fp32 scores; packs bf16 pairs into
+// pk and returns the fp32 sum of the p_c.
+__device__ __forceinline__ float exp2_pack32(const uint32_t (&sv)[32], float scale, float negm,
+                                             uint32_t (&pk)[16]) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 32; c += 4) {
+    float x0, x1, x2, x3;
+    fma_f32x2(x0, x1, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), scale, scale, negm, negm);
+    fma_f32x2(x2, x3, __uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]), scale, scale, negm, negm);
+    x0 = fast_exp2(x0); x1 = fast_exp2(x1); x2 = fast_exp2(x2); x3 = fast_exp2(x3);
+    pk[c / 2] = pack_bf16x2(x0, x1);
+    pk[c / 2 + 1] = pack_bf16x2(x2, x3);
+    add_f32x2(s0, s1, s0, s1, x0, x1);
+    add_f32x2(s2, s3, s2, s3, x2, x3);
+  }
+  return (s0 + s1) + (s2 + s3);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
