@@ -31,6 +31,107 @@ struct SelectDims {
   int D;
 };
 
+// Top-NS of one row of order keys, by one warp: 4-pass radix select of the
+// NS-th largest key, ties at that key taken by ascending block index, then
+// every winner placed at its rank (key descending, index ascending).  Writes
+// the row's indices and, when sel_mask is non-NULL, its selection bitmask.
+__device__ __forceinline__ void row_topk(const uint32_t* rk, int64_t NT, int64_t NG, int64_t NS, uint32_t* h,
+                                         uint32_t* mw, uint64_t* cl, int32_t* out, uint32_t* mask_out) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0, pmask = 0;
+  uint32_t remaining = uint32_t(NS);
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = lane; b < 256; b += 32) h[b] = 0;
+    __syncwarp();
+    for (int64_t j = lane; j < NT; j += 32) {
+      const uint32_t kj = rk[j];
+      if ((kj & pmask) == prefix) atomicAdd(&h[(kj >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    // lane owns buckets 255-8*lane ... 248-8*lane (descending)
+    uint32_t cnt[8], tot = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) { cnt[u] = h[255 - 8 * lane - u]; tot += cnt[u]; }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    const uint32_t excl = incl - tot;
+    const uint32_t hit = __ballot_sync(0xffffffffu, incl >= remaining);
+    const int src = __ffs(hit) - 1;  // first lane whose range reaches `remaining`
+    uint32_t bucket = 0, above = 0;
+    if (lane == src) {
+      uint32_t c = excl;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (c + cnt[u] >= remaining) { bucket = 255 - 8 * lane - u; above = c; break; }
+        c += cnt[u];
+      }
+    }
+    bucket = __shfl_sync(0xffffffffu, bucket, src);
+    above = __shfl_sync(0xffffffffu, above, src);
+    remaining -= above;
+    prefix |= bucket << shift;
+    pmask |= 0xFFu << shift;
+    __syncwarp();
+  }
+  const uint32_t kth = prefix;  // key of the NS-th largest score
+  // ties at kth: take the `remaining` lowest block indices
+  uint32_t taken = 0;
+  for (int64_t j0 = 0; j0 < NT; j0 += 32) {
+    const int64_t j = j0 + lane;
+    const uint32_t kj = (j < NT) ? rk[j] : 0u;
+    const bool eq = (j < NT) && (kj == kth);
+    const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
+    const uint32_t rank_eq = taken + __popc(eqb & ((1u << lane) - 1u));
+    const bool sel = (j < NT) && (kj > kth || (eq && rank_eq < remaining));
+    const uint32_t selb = __ballot_sync(0xffffffffu, sel);
+    taken += __popc(eqb);
+    if (lane == 0) mw[j0 >> 5] = selb;  // j0 is a multiple of 32: one word per step
+  }
+  __syncwarp();
+
+  if (NS <= kCompactMax) {
+    // compact (key, index) of the selected blocks, then place by rank
+    uint32_t base = 0;
+    for (int64_t j0 = 0; j0 < NT; j0 += 32) {
+      const int64_t j = j0 + lane;
+      const bool sel = (mw[j0 >> 5] >> lane) & 1u;
+      const uint32_t b = __ballot_sync(0xffffffffu, sel);
+      if (sel) {
+        const uint32_t pos = base + __popc(b & ((1u << lane) - 1u));
+        // larger composite = better: key, then lower index
+        cl[pos] = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
+      }
+      base += __popc(b);
+    }
+    __syncwarp();
+    for (int64_t e = lane; e < NS; e += 32) {
+      const uint64_t me = cl[e];
+      int64_t rank = 0;
+      for (int64_t f = 0; f < NS; ++f) rank += (cl[f] > me) ? 1 : 0;
+      out[rank] = int32_t(0xFFFFFFFFu - uint32_t(me & 0xFFFFFFFFu));
+    }
+  } else {
+    for (int64_t j = lane; j < NT; j += 32) {
+      if (!((mw[j >> 5] >> (j & 31)) & 1u)) continue;
+      const uint64_t me = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
+      int64_t rank = 0;
+      for (int64_t f = 0; f < NT; ++f) {
+        if (!((mw[f >> 5] >> (f & 31)) & 1u)) continue;
+        const uint64_t o = (uint64_t(rk[f]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(f));
+        rank += (o > me) ? 1 : 0;
+      }
+      out[rank] = int32_t(j);
+    }
+  }
+  if (mask_out)
+    for (int64_t w = lane; w < NG; w += 32) mask_out[w] = mw[w];
+}
+
 // Dynamic shared memory: qrow[kRows][D] f32 | kch[kChunk][D+1] f32 |
 // keys[kRows][NT] u32 | hist[kRows][256] u32 | mask[kRows][NG] u32 |
 // compact[kRows][NS] u64 (when NS <= kCompactMax)
@@ -100,108 +201,169 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   // ---- per-row radix select + rank placement (one warp per row) --------
   if (warp >= nrows) return;
   const int64_t row = i0 + warp;
-  const uint32_t* rk = keys + warp * NT;
-  uint32_t* h = hist + warp * 256;
-  uint32_t* mw = maskw + warp * NG;
+  row_topk(keys + warp * NT, NT, NG, NS, hist + warp * 256, maskw + warp * NG, compact + int64_t(warp) * NS,
+           indices + (bh * NT + row) * NS, sel_mask ? sel_mask + (bh * NT + row) * NG : nullptr);
+}
 
-  uint32_t prefix = 0, pmask = 0;
-  uint32_t remaining = uint32_t(NS);
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int b = lane; b < 256; b += 32) h[b] = 0;
-    __syncwarp();
-    for (int64_t j = lane; j < NT; j += 32) {
-      const uint32_t kj = rk[j];
-      if ((kj & pmask) == prefix) atomicAdd(&h[(kj >> shift) & 255u], 1u);
-    }
-    __syncwarp();
-    // lane owns buckets 255-8*lane ... 248-8*lane (descending)
-    uint32_t cnt[8], tot = 0;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) { cnt[u] = h[255 - 8 * lane - u]; tot += cnt[u]; }
-    uint32_t incl = tot;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += y;
-    }
-    const uint32_t excl = incl - tot;
-    const uint32_t hit = __ballot_sync(0xffffffffu, incl >= remaining);
-    const int src = __ffs(hit) - 1;  // first lane whose range reaches `remaining`
-    uint32_t bucket = 0, above = 0;
-    if (lane == src) {
-      uint32_t c = excl;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (c + cnt[u] >= remaining) { bucket = 255 - 8 * lane - u; above = c; break; }
-        c += cnt[u];
-      }
-    }
-    bucket = __shfl_sync(0xffffffffu, bucket, src);
-    above = __shfl_sync(0xffffffffu, above, src);
-    remaining -= above;
-    prefix |= bucket << shift;
-    pmask |= 0xFFu << shift;
-    __syncwarp();
-  }
-  const uint32_t kth = prefix;  // key of the NS-th largest score
-  // ties at kth: take the `remaining` lowest block indices
-  for (int64_t w = lane; w < NG; w += 32) mw[w] = 0;
-  __syncwarp();
-  uint32_t taken = 0;
-  for (int64_t j0 = 0; j0 < NT; j0 += 32) {
-    const int64_t j = j0 + lane;
-    const uint32_t kj = (j < NT) ? rk[j] : 0u;
-    const bool eq = (j < NT) && (kj == kth);
-    const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
-    const uint32_t rank_eq = taken + __popc(eqb & ((1u << lane) - 1u));
-    const bool sel = (j < NT) && (kj > kth || (eq && rank_eq < remaining));
-    const uint32_t selb = __ballot_sync(0xffffffffu, sel);
-    taken += __popc(eqb);
-    if (lane == 0) mw[j0 >> 5] = selb;  // j0 is a multiple of 32: one word per step
-  }
-  __syncwarp();
 
-  int32_t* out = indices + (bh * NT + row) * NS;
-  if (NS <= kCompactMax) {
-    // compact (key, index) of the selected blocks, then place by rank
-    uint64_t* cl = compact + int64_t(warp) * NS;
-    uint32_t base = 0;
-    for (int64_t j0 = 0; j0 < NT; j0 += 32) {
-      const int64_t j = j0 + lane;
-      const bool sel = (mw[j0 >> 5] >> lane) & 1u;
-      const uint32_t b = __ballot_sync(0xffffffffu, sel);
-      if (sel) {
-        const uint32_t pos = base + __popc(b & ((1u << lane) - 1u));
-        // larger composite = better: key, then lower index
-        cl[pos] = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
+// ---------------------------------------------------------------------------
+// bf16: scores on the tensor cores (mma.sync, fp32 accumulation, rounded to
+// bf16 like the reference's bf16 einsum), 16 query blocks per CTA.
+// ---------------------------------------------------------------------------
+namespace sel_tc {
+constexpr int kRowsTC = 16;      // query blocks per CTA, one warp each for the top-k
+constexpr int kThreadsTC = 512;
+constexpr int kKeyChunk = 128;   // key blocks per scoring pass: 16 warps x 8
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+template <int D>
+struct Layout {
+  static constexpr int kRS = D + 8;  // padded row stride (elements): conflict-free ldmatrix
+  __host__ __device__ static size_t bytes(int64_t NT, int64_t NG, int64_t NS, size_t* off) {
+    size_t o = 0;
+    off[0] = o; o += size_t(kRowsTC) * kRS * 2;           // qs  bf16 [16][RS]
+    off[1] = o; o += size_t(kKeyChunk) * kRS * 2;         // ks  bf16 [128][RS]
+    off[2] = o; o += size_t(kKeyChunk) * 4;               // bias f32 [128]
+    off[3] = o; o += size_t(kRowsTC) * NT * 4;            // keys u32 [16][NT]
+    off[4] = o; o += size_t(kRowsTC) * 256 * 4;           // hist
+    off[5] = o; o += size_t(kRowsTC) * NG * 4;            // mask words
+    o = (o + 7) & ~size_t(7);
+    off[6] = o; if (NS <= kCompactMax) o += size_t(kRowsTC) * NS * 8;  // compact lists
+    return o;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreadsTC, 1) select_tc_kernel(
+    const __nv_bfloat16* __restrict__ qc, const __nv_bfloat16* __restrict__ kc, const float* __restrict__ h_norm,
+    const float* __restrict__ noise, SelectDims dm, float scale, int use_cov_bias,
+    int32_t* __restrict__ indices, uint32_t* __restrict__ sel_mask) {
+  using L = Layout<D>;
+  constexpr int RS = L::kRS;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t NT = dm.NT, NG = dm.NG, NTP = dm.NTP, NS = dm.NS;
+  size_t off[7];
+  L::bytes(NT, NG, NS, off);
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw + off[0]);
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw + off[1]);
+  float* bias = reinterpret_cast<float*>(smem_raw + off[2]);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + off[3]);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem_raw + off[4]);
+  uint32_t* maskw = reinterpret_cast<uint32_t*>(smem_raw + off[5]);
+  uint64_t* compact = reinterpret_cast<uint64_t*>(smem_raw + off[6]);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t bh = blockIdx.y;
+  const int64_t i0 = int64_t(blockIdx.x) * kRowsTC;
+  const int nrows = int((NT - i0 < kRowsTC) ? (NT - i0) : int64_t(kRowsTC));
+  const float scale32 = scale;
+  constexpr int kVec = D / 8;
+
+  for (int x = tid; x < kRowsTC * kVec; x += kThreadsTC) {
+    const int r = x / kVec, c = x % kVec;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < nrows) val = reinterpret_cast<const uint4*>(qc + (bh * NTP + i0 + r) * D)[c];
+    *reinterpret_cast<uint4*>(qs + r * RS + c * 8) = val;
+  }
+
+  const int gq = lane >> 2, tq = lane & 3;
+  for (int64_t j0 = 0; j0 < NT; j0 += kKeyChunk) {
+    __syncthreads();
+    // kc * scale rounded to bf16 (:365), staged for the MMA
+    for (int x = tid; x < kKeyChunk * kVec; x += kThreadsTC) {
+      const int jj = x / kVec, c = x % kVec;
+      uint4 out = make_uint4(0, 0, 0, 0);
+      if (j0 + jj < NT) {
+        const uint4 in = reinterpret_cast<const uint4*>(kc + (bh * NTP + j0 + jj) * D)[c];
+        const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+          o[e] = pack_bf16x2(f.x * scale32, f.y * scale32);
+        }
+        out = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      base += __popc(b);
+      *reinterpret_cast<uint4*>(ks + jj * RS + c * 8) = out;
     }
-    __syncwarp();
-    for (int64_t e = lane; e < NS; e += 32) {
-      const uint64_t me = cl[e];
-      int64_t rank = 0;
-      for (int64_t f = 0; f < NS; ++f) rank += (cl[f] > me) ? 1 : 0;
-      out[rank] = int32_t(0xFFFFFFFFu - uint32_t(me & 0xFFFFFFFFu));
-    }
-  } else {
-    for (int64_t j = lane; j < NT; j += 32) {
-      if (!((mw[j >> 5] >> (j & 31)) & 1u)) continue;
-      const uint64_t me = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
-      int64_t rank = 0;
-      for (int64_t f = 0; f < NT; ++f) {
-        if (!((mw[f >> 5] >> (f & 31)) & 1u)) continue;
-        const uint64_t o = (uint64_t(rk[f]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(f));
-        rank += (o > me) ? 1 : 0;
+    if (tid < kKeyChunk) {
+      const int64_t j = j0 + tid;
+      float b = 0.f;
+      if (use_cov_bias && j < NT) {
+        b = logf(h_norm[bh * NT + j] + 1e-6f);  // :368
+        if (noise) b = b + noise[bh * NT + j];  // :370
       }
-      out[rank] = int32_t(j);
+      bias[tid] = b;
+    }
+    __syncthreads();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int kb = warp * 8;  // this warp's 8 key blocks within the chunk
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4], b[2];
+      {
+        const int mat = lane >> 3, i = lane & 7;
+        ldsm_x4(a, qs + (i + ((mat & 1) ? 8 : 0)) * RS + kk * 16 + ((mat >= 2) ? 8 : 0));
+      }
+      {
+        const int mat = (lane >> 3) & 1, i = lane & 7;
+        ldsm_x2(b, ks + (kb + i) * RS + kk * 16 + mat * 8);
+      }
+      mma16816(acc, a, b);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = gq + ((e >= 2) ? 8 : 0);
+      const int key = kb + 2 * tq + (e & 1);
+      const int64_t j = j0 + key;
+      if (r < nrows && j < NT) {
+        float sc = Elem<__nv_bfloat16>::round(acc[e]);  // einsum output in bf16
+        if (use_cov_bias) sc = sc + bias[key];          // :371
+        keys[r * NT + j] = order_key(sc);
+      }
     }
   }
-  if (sel_mask) {
-    uint32_t* mo = sel_mask + (bh * NT + row) * NG;
-    for (int64_t w = lane; w < NG; w += 32) mo[w] = mw[w];
-  }
+  __syncthreads();
+  if (warp >= nrows) return;
+  const int64_t row = i0 + warp;
+  row_topk(keys + warp * NT, NT, NG, NS, hist + warp * 256, maskw + warp * NG, compact + int64_t(warp) * NS,
+           indices + (bh * NT + row) * NS, sel_mask ? sel_mask + (bh * NT + row) * NG : nullptr);
+}
+}  // namespace sel_tc
+
+template <int D>
+static size_t select_tc_smem(const SelectDims& dm) {
+  size_t off[7];
+  return sel_tc::Layout<D>::bytes(dm.NT, dm.NG, dm.NS, off);
+}
+
+template <int D>
+static cudaError_t launch_select_tc_t(cudaStream_t st, const void* qc, const void* kc, const float* hn,
+                                      const float* noise, int64_t BH, SelectDims dm, float scale, int use_cov_bias,
+                                      int32_t* idx, uint32_t* mask) {
+  const size_t smem = select_tc_smem<D>(dm);
+  auto kern = sel_tc::select_tc_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid{unsigned(cdiv(dm.NT, sel_tc::kRowsTC)), unsigned(BH), 1u};
+  kern<<<grid, sel_tc::kThreadsTC, smem, st>>>(static_cast<const __nv_bfloat16*>(qc),
+                                               static_cast<const __nv_bfloat16*>(kc), hn, noise, dm, scale,
+                                               use_cov_bias, idx, mask);
+  return cudaGetLastError();
 }
 
 size_t select_smem_bytes(int D, int64_t NT, int64_t NG, int64_t NS) {
@@ -232,6 +394,11 @@ cudaError_t launch_select(cudaStream_t st, int dtype, int D, const void* qc, con
   SelectDims dm;
   dm.NT = NT; dm.NG = cdiv(NT, kGroup); dm.NTP = dm.NG * kGroup; dm.NS = NS; dm.D = D;
   if (dtype == PASA_BF16) {
+    constexpr size_t kMaxSmem = 227 * 1024;
+    if (D == 64 && select_tc_smem<64>(dm) <= kMaxSmem)
+      return launch_select_tc_t<64>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+    if (D == 128 && select_tc_smem<128>(dm) <= kMaxSmem)
+      return launch_select_tc_t<128>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
     if (D == 64) return launch_select_t<__nv_bfloat16, 64>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
     return launch_select_t<__nv_bfloat16, 128>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
   }
