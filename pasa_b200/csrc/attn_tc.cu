@@ -12,20 +12,24 @@
 // B200 mapping:
 //   * a CTA owns a PAIR of adjacent 64-query blocks (128 rows), so every MMA
 //     is M=128 (the full tcgen05 datapath).  Phase 1 walks the union of the
-//     two blocks' selected key blocks in ascending order; rows whose block
-//     did not select the key block get P = 0 and skip the exponentials.
-//     Phase 2 (shared by both blocks) walks the 32-block groups with each
-//     half's own selection bits.
-//   * warp 0: TMA producer (Q once, then K/V blocks or kc/vc/H_g of a group
-//     per step through a ring of stages); warp 1: TMEM owner and MMA issuer
-//     (one thread); warps 2-9: softmax, two threads per query row (TMEM
-//     lane), each owning half of the row's columns; the two partner warps
-//     exchange row maxima and probability sums through shared memory.
-//   * TMEM: O accumulator (D cols), two S/P buffers (64 cols; P is written
-//     back as packed bf16 over S), two U buffers (D/2 cols).  The first-order
-//     term is an MMA: U = bf16(w_t * q_t) (A operand from TMEM, w_t = scale *
-//     sum of the group's probabilities) times H_g (B from shared memory),
-//     accumulated straight into O.
+//     two blocks' selected key blocks in ascending order, TWO key blocks per
+//     step: the score MMA is N=128 (full rate; N=64 runs at ~55%) and P.V is
+//     K=128.  Rows whose query block did not select a key block get P = 0
+//     and skip its exponentials.  Phase 2 (shared by both query blocks) walks
+//     the 32-block groups with each half's own selection bits.
+//   * Q lives in TMEM as the A operand of every score MMA, so shared memory
+//     carries only K/V (or kc/vc/H) tiles: TMA writes them once, the tensor
+//     core reads them once.
+//   * warp 0: TMA producer (ring 1: K/V of block pairs, 3 slots; ring 2,
+//     aliased on the same memory: kc/vc rows and H of a group); warp 1: TMEM
+//     owner and MMA issuer (one thread, non-blocking event loop); warps 2-9:
+//     softmax, two threads per query row (TMEM lane), each owning half of
+//     every key block's columns; partner warps exchange row maxima and
+//     probability sums through shared memory.
+//   * TMEM: O (fp32), Q (bf16), two S buffers of 128 columns.  P is written
+//     back over S as packed bf16; in phase 2 the first-order operand
+//     U = bf16(w_t q_t) (w_t = scale * sum of the group's probabilities) sits
+//     in the S buffer's upper half and U.H_g is accumulated straight into O.
 //   * softmax rescales O only when a row max grows by more than 2^8
 //     (exact either way: O and l share the stale max); the exact running max
 //     is tracked separately to reproduce g_l.
@@ -54,35 +58,38 @@ struct Cfg {
   static constexpr int kKVBytes = kBlock * D * 2;       // one K (or V) block
   static constexpr int kCBytes = kGroup * D * 2;        // kc (or vc) rows of one group
   static constexpr int kHBytes = D * D * 2;
-  // one shared-memory region holds two rings, used one after the other:
-  // ring 1 (phase 1) slots hold K and V of a block, ring 2 (phase 2) slots
-  // hold kc, vc rows and H of a group
-  static constexpr int kSlot1 = 2 * kKVBytes;
+  // ring 1 (phase 1) slots: K of two blocks, then V of two blocks, each as
+  // kBoxes boxes of [128 rows][64 cols]; ring 2 (phase 2) slots, aliased on
+  // the same memory: kc rows, vc rows, H of one group
+  static constexpr int kSlot1 = 4 * kKVBytes;
   static constexpr int kSlot2 = 2 * kCBytes + kHBytes;
-  static constexpr int kRingBytes = (D == 128) ? 5 * kSlot1 : 8 * kSlot1;
-  static constexpr int kS1 = kRingBytes / kSlot1;
+  static constexpr int kS1 = 3;
+  static constexpr int kRingBytes = kS1 * kSlot1;
   static constexpr int kS2 = kRingBytes / kSlot2;
+  static constexpr int kPairBox = 2 * kBlock * 128;     // one [128 rows][64 cols] box
   static constexpr uint32_t kTxP1 = kSlot1;
   static constexpr uint32_t kTxP2 = kSlot2;
-  // TMEM columns: O (fp32), Q (packed bf16, the A operand of every score
-  // MMA), three S/P buffers, two U buffers
+  // TMEM columns
   static constexpr uint32_t kColO = 0;
   static constexpr uint32_t kColQ = 128;
-  static constexpr uint32_t kColS0 = 192;
-  static constexpr uint32_t kColU0 = 384;
+  static constexpr uint32_t kColS0 = 192;               // S buffer b at kColS0 + 128 b
+  static constexpr uint32_t kColU = 64;                 // phase 2: U inside the S buffer
   static constexpr uint32_t kTmemCols = 512;
-  // shared memory carve-up (offsets from a 1024-aligned base)
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffRing = kQBytes;
-  static constexpr int kOffUnion = kOffRing + kRingBytes;             // u16 [kMaxNT]
-  static constexpr int kOffMask = kOffUnion + kMaxNT * 2;              // u32 [2][kMaxNG]
+  // shared memory carve-up (offsets from a 1024-aligned base).  Q is staged
+  // inside ring slot 2 and copied to TMEM before that slot is first filled.
+  static constexpr int kOffRing = 0;
+  static constexpr int kOffQ = 2 * kSlot1;
+  static constexpr int kOffUnion = kOffRing + kRingBytes;            // u16 [kMaxNT]
+  static constexpr int kOffMask = kOffUnion + kMaxNT * 2;            // u32 [2][kMaxNG]
   static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][2 halves][128]
   static constexpr int kOffBar = kOffXch + 2 * 2 * kRowsPerTile * 4;
-  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 1 + 1 + 3 + 3 + 2;
+  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 2 + 2 + 2 + 2;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
-  static_assert(kS1 >= 3 && kS2 >= 2, "ring too small");
-  static_assert(kColU0 + 2 * 64 <= kTmemCols, "TMEM budget");
+  static_assert(kOffQ + kQBytes <= kRingBytes, "Q staging must fit in the ring");
+  static_assert(kS2 >= 2, "ring too small");
+  static_assert(kColS0 + 2 * 128 <= kTmemCols, "TMEM budget");
+  static_assert(kColU + D / 2 <= 128, "U must fit in the S buffer");
 };
 
 struct Maps {
@@ -100,7 +107,7 @@ struct Params {
 // Optional step tracer (compile with -DPASA_TRACE): the CTA at grid (0, 0)
 // records SM clock stamps of its pipeline events for the first kTraceSteps
 // steps into g_pasa_trace[event][step]: 0 producer issue, 1 S issue, 2 P.V
-// issue, 4+w softmax warp w sees S, 12+w softmax warp w done;
+// issue, 3 data landed, 4+w softmax warp w sees S, 12+w softmax warp w done;
 // pasa_trace_read() copies them out.
 #ifdef PASA_TRACE
 constexpr int kTraceSteps = 1024;
@@ -118,6 +125,13 @@ __device__ __forceinline__ void report(uint32_t* err) {
   if (err) atomicOr(err, PASA_DEVERR_WAIT_TIMEOUT);
 }
 
+// Set the raw fp32 scores of columns c >= nvalid to -inf.
+__device__ __forceinline__ void mask_tail32(uint32_t (&sv)[32], int nvalid) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_constant__ Maps maps, Params P) {
   using C = Cfg<D>;
@@ -125,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint16_t* ulist = reinterpret_cast<uint16_t*>(sm + C::kOffUnion);  // (block << 2) | half bits
   uint32_t* maskw = reinterpret_cast<uint32_t*>(sm + C::kOffMask);  // [2][kMaxNG]
+  float* xch = reinterpret_cast<float*>(sm + C::kOffXch);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
   uint64_t* full1 = bars;
   uint64_t* empty1 = full1 + C::kS1;
@@ -132,11 +147,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* empty2 = full2 + C::kS2;
   uint64_t* q_full = empty2 + C::kS2;
   uint64_t* q_tmem = q_full + 1;   // Q copied into TMEM by the softmax warps
-  uint64_t* s_full = q_tmem + 1;   // [3]
-  uint64_t* p_ready = s_full + 3;  // [3]
-  uint64_t* o_done = p_ready + 3;  // [2]
+  uint64_t* s_full = q_tmem + 1;   // [2]
+  uint64_t* p_ready = s_full + 2;  // [2]
+  uint64_t* o_done = p_ready + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffSlot);
-  float* xch = reinterpret_cast<float*>(sm + C::kOffXch);
   __shared__ uint32_t s_nu;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -151,8 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     for (int s = 0; s < C::kS2; ++s) { mbar_init(&full2[s], 1); mbar_init(&empty2[s], 1); }
     mbar_init(q_full, 1);
     mbar_init(q_tmem, 8);
-    for (int b = 0; b < 3; ++b) { mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], 8); }
-    for (int b = 0; b < 2; ++b) mbar_init(&o_done[b], 1);
+    for (int b = 0; b < 2; ++b) { mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], 8); mbar_init(&o_done[b], 1); }
     fence_barrier_init();
   }
   if (warp == 1) { tmem_alloc(tmem_slot, C::kTmemCols); tmem_relinquish(); }
@@ -195,13 +208,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int64_t nU = s_nu;
-  const int64_t total = nU + NG;
+  const int64_t nP = (nU + 1) / 2;  // phase-1 steps: two union blocks each (a lone last block pairs with itself)
+  const int64_t total = nP + NG;
 
   if (warp == 0) {
     // ================= TMA producer =================
 #ifdef PASA_TRACE
     if (lane == 1 && blockIdx.x == 0 && blockIdx.y == 0) {  // trace only: stamp data arrival (event 3)
-      for (int64_t n = 0; n < nU && n < kTraceSteps; ++n)
+      for (int64_t n = 0; n < nP && n < kTraceSteps; ++n)
         if (mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)) PASA_TRACE_MARK(3, n);
     }
 #endif
@@ -212,29 +226,39 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       mbar_arrive_expect_tx(q_full, C::kQBytes);
       for (int bx = 0; bx < C::kBoxes; ++bx)
         tma_load_3d(sm + C::kOffQ + bx * (kRowsPerTile * 128), &maps.q, q_full, bx * 64, row0, int32_t(bh));
-      // Phase 1: K and V of every union block through ring 1
-      for (int64_t n = 0; n < nU && ok; ++n) {
-        const int s = int(n % C::kS1);
-        if (!mbar_wait_bounded(&empty1[s], uint32_t((n / C::kS1) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
-        PASA_TRACE_MARK(0, n);
+      bool q_released = false;  // Q's staging area (ring slot 2) is free once Q sits in TMEM
+      auto release_q = [&]() {
+        if (!q_released) { ok = ok && mbar_wait_bounded(q_tmem, 0, kPollLimit); q_released = true; }
+      };
+      // Phase 1: K and V of every union block pair through ring 1
+      for (int64_t p = 0; p < nP && ok; ++p) {
+        const int s = int(p % C::kS1);
+        if (!mbar_wait_bounded(&empty1[s], uint32_t((p / C::kS1) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
+        if (s == 2) { release_q(); if (!ok) break; }
+        PASA_TRACE_MARK(0, p);
         unsigned char* st = sm + C::kOffRing + s * C::kSlot1;
-        const int32_t j = int32_t(ulist[n] >> 2);
+        const int32_t j0 = int32_t(ulist[2 * p] >> 2);
+        const int32_t j1 = (2 * p + 1 < nU) ? int32_t(ulist[2 * p + 1] >> 2) : j0;
         mbar_arrive_expect_tx(&full1[s], C::kTxP1);
         for (int bx = 0; bx < C::kBoxes; ++bx) {
-          tma_load_3d(st + bx * (kBlock * 128), &maps.k, &full1[s], bx * 64, j * kBlock, int32_t(bh));
-          tma_load_3d(st + C::kKVBytes + bx * (kBlock * 128), &maps.v, &full1[s], bx * 64, j * kBlock,
-                      int32_t(bh));
+          unsigned char* kb = st + bx * C::kPairBox;
+          unsigned char* vb = st + 2 * C::kKVBytes + bx * C::kPairBox;
+          tma_load_3d(kb, &maps.k, &full1[s], bx * 64, j0 * kBlock, int32_t(bh));
+          tma_load_3d(kb + kBlock * 128, &maps.k, &full1[s], bx * 64, j1 * kBlock, int32_t(bh));
+          tma_load_3d(vb, &maps.v, &full1[s], bx * 64, j0 * kBlock, int32_t(bh));
+          tma_load_3d(vb + kBlock * 128, &maps.v, &full1[s], bx * 64, j1 * kBlock, int32_t(bh));
         }
-        issued = n + 1;
+        issued = p + 1;
       }
-      // ring 2 aliases ring 1: every phase-1 slot must be released first
-      for (int64_t n = (nU > C::kS1 ? nU - C::kS1 : 0); n < nU && ok; ++n)
-        if (!mbar_wait_bounded(&empty1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)) ok = false;
+      // ring 2 aliases ring 1 (and Q's staging area): all of it must be free
+      for (int64_t p = (nP > C::kS1 ? nP - C::kS1 : 0); p < nP && ok; ++p)
+        if (!mbar_wait_bounded(&empty1[p % C::kS1], uint32_t((p / C::kS1) & 1), kPollLimit)) ok = false;
+      if (ok) release_q();
       // Phase 2: kc, vc rows and H of every group through ring 2
       for (int64_t g = 0; g < NG && ok; ++g) {
         const int s = int(g % C::kS2);
         if (!mbar_wait_bounded(&empty2[s], uint32_t((g / C::kS2) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
-        PASA_TRACE_MARK(0, nU + g);
+        PASA_TRACE_MARK(0, nP + g);
         unsigned char* st = sm + C::kOffRing + s * C::kSlot2;
         mbar_arrive_expect_tx(&full2[s], C::kTxP2);
         for (int bx = 0; bx < C::kBoxes; ++bx) {
@@ -243,74 +267,69 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                       int32_t(bh));
           tma_load_3d(st + 2 * C::kCBytes + bx * (D * 128), &maps.h, &full2[s], bx * 64, 0, int32_t(bh * NG + g));
         }
-        issued = nU + g + 1;
+        issued = nP + g + 1;
       }
       if (!ok) report(P.err);
       // drain: let this thread's last copies land before the CTA can exit
       for (int64_t n = (issued > 3 ? issued - 3 : 0); n < issued; ++n) {
-        if (n < nU) mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit);
-        else mbar_wait_bounded(&full2[(n - nU) % C::kS2], uint32_t(((n - nU) / C::kS2) & 1), kPollLimit);
+        if (n < nP) mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit);
+        else mbar_wait_bounded(&full2[(n - nP) % C::kS2], uint32_t(((n - nP) / C::kS2) & 1), kPollLimit);
       }
     }
   } else if (warp == 1) {
     // ================= MMA issuer =================
-    // S of step n+2 is issued before P.V of step n, so the softmax never
-    // waits for its scores; S/P and U buffers rotate over three slots.
     if (lane == 0) {
-      constexpr uint32_t idS64 = umma_idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idS128 = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idS32 = umma_idesc_bf16(128, 32, false, false);
       constexpr uint32_t idPV = umma_idesc_bf16(128, D, false, true);
       bool ok = mbar_wait_bounded(q_tmem, 0, kPollLimit);
       tc_fence_after();
+      const uint32_t tQ = tmem + C::kColQ;
 
       auto slot_addr = [&](int64_t n) -> uint32_t {
-        return (n < nU) ? smem_u32(sm + C::kOffRing + int(n % C::kS1) * C::kSlot1)
-                        : smem_u32(sm + C::kOffRing + int((n - nU) % C::kS2) * C::kSlot2);
+        return (n < nP) ? smem_u32(sm + C::kOffRing + int(n % C::kS1) * C::kSlot1)
+                        : smem_u32(sm + C::kOffRing + int((n - nP) % C::kS2) * C::kSlot2);
       };
-      // Event loop: issue whichever of the next S (scores, needs its TMA
-      // data) or the next P.V (needs the softmax) is ready, never blocking
-      // one on the other.  P.V completion releases ring slots, so P.V goes
-      // first when both are ready.  S runs at most two steps ahead of P.V
-      // (three S/P buffers).  Ring 2 reuses ring 1's memory, so group scores
-      // wait until every exact-block P.V is issued.
       auto data_ready = [&](int64_t n) -> bool {
-        if (n < nU) return mbar_test(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1));
-        const int64_t g = n - nU;
+        if (n < nP) return mbar_test(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1));
+        const int64_t g = n - nP;
         return mbar_test(&full2[g % C::kS2], uint32_t((g / C::kS2) & 1));
       };
       auto issue_s = [&](int64_t n) {
         PASA_TRACE_MARK(1, n);
         tc_fence_after();
         const uint32_t st = slot_addr(n);
-        const int b = int(n % 3);
-        const uint32_t tS = tmem + C::kColS0 + 64u * b;
-        const int rows = (n < nU) ? kBlock : kGroup;
-        const uint32_t id = (n < nU) ? idS64 : idS32;
+        const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(n & 1);
+        if (n < nP) {  // S = Q . [K_j0; K_j1]^T, N = 128
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int bx = kk / 4, ko = (kk % 4) * 32;
-          const uint64_t bd = umma_desc_sw128(st + bx * (rows * 128) + ko, 16, 1024);
-          mma_ts(tS, tmem + C::kColQ + kk * 8, bd, id, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int bx = kk / 4, ko = (kk % 4) * 32;
+            const uint64_t bd = umma_desc_sw128(st + bx * C::kPairBox + ko, 16, 1024);
+            mma_ts(tS, tQ + kk * 8, bd, idS128, kk > 0 ? 1u : 0u);
+          }
+        } else {       // S = Q . kc_g^T, N = 32
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int bx = kk / 4, ko = (kk % 4) * 32;
+            const uint64_t bd = umma_desc_sw128(st + bx * (kGroup * 128) + ko, 16, 1024);
+            mma_ts(tS, tQ + kk * 8, bd, idS32, kk > 0 ? 1u : 0u);
+          }
         }
-        PASA_TRACE_MARK(20, n);
-        tc_commit(&s_full[b]);
-        PASA_TRACE_MARK(21, n);
+        tc_commit(&s_full[n & 1]);
       };
       auto issue_pv = [&](int64_t m) {
-        const int b = int(m % 3);
         PASA_TRACE_MARK(2, m);
         tc_fence_after();
         const uint32_t st = slot_addr(m);
-        const uint32_t tS = tmem + C::kColS0 + 64u * b;
-        const uint32_t tU = tmem + C::kColU0 + 64u * uint32_t(m & 1);
-        if (m < nU) {
+        const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(m & 1);
+        if (m < nP) {  // O += P . [V_j0; V_j1], K = 128
 #pragma unroll
-          for (int kk = 0; kk < kBlock / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(st + C::kKVBytes + kk * 2048, C::kKVBytes / C::kBoxes, 1024);
+          for (int kk = 0; kk < 2 * kBlock / 16; ++kk) {
+            const uint64_t bd = umma_desc_sw128(st + 2 * C::kKVBytes + kk * 2048, C::kPairBox, 1024);
             mma_ts(tmem + C::kColO, tS + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty1[m % C::kS1]);
-        } else {
+        } else {       // O += P_g . vc_g + U_g . H_g
 #pragma unroll
           for (int kk = 0; kk < kGroup / 16; ++kk) {
             const uint64_t bd = umma_desc_sw128(st + C::kCBytes + kk * 2048, C::kCBytes / C::kBoxes, 1024);
@@ -319,33 +338,33 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t bd = umma_desc_sw128(st + 2 * C::kCBytes + kk * 2048, C::kHBytes / C::kBoxes, 1024);
-            mma_ts(tmem + C::kColO, tU + kk * 8, bd, idPV, 1u);
+            mma_ts(tmem + C::kColO, tS + C::kColU + kk * 8, bd, idPV, 1u);
           }
-          tc_commit(&empty2[(m - nU) % C::kS2]);
+          tc_commit(&empty2[(m - nP) % C::kS2]);
         }
-        PASA_TRACE_MARK(22, m);
         tc_commit(&o_done[m & 1]);
-        PASA_TRACE_MARK(23, m);
       };
 
+      // Event loop: issue whichever of the next S (needs its TMA data) or the
+      // next P.V (needs the softmax) is ready.  S runs at most one step ahead
+      // of P.V (two S buffers).  Ring 2 reuses ring 1's memory, so group
+      // scores wait until every phase-1 P.V is issued.
       int64_t ns = 0, npv = 0;
       uint64_t idle_since = 0;
       while (ok && npv < total) {
         bool progressed = false;
-        if (npv < ns && mbar_test(&p_ready[npv % 3], uint32_t((npv / 3) & 1))) {
+        if (npv < ns && mbar_test(&p_ready[npv & 1], uint32_t((npv >> 1) & 1))) {
           issue_pv(npv++);
           progressed = true;
         }
-        // phase 2 runs one step ahead only: its U buffers are double, not triple
-        if (ns < total && (ns < nU ? ns <= npv + 2 : (npv >= nU && ns <= npv + 1)) && data_ready(ns)) {
+        if (ns < total && ns <= npv + 1 && (ns < nP || npv >= nP) && data_ready(ns)) {
           issue_s(ns++);
           progressed = true;
         }
         if (progressed) {
           idle_since = 0;
         } else {
-          // back off: this warp shares its SM sub-partition with two softmax warps
-          __nanosleep(32);
+          __nanosleep(32);  // this warp shares its SM sub-partition with two softmax warps
           if (idle_since == 0) idle_since = sm_cycles();
           else if (sm_cycles() - idle_since > kPollLimit) ok = false;
         }
@@ -355,9 +374,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     __syncwarp();
   } else {
     // ================= softmax / correction (warps 2..9) =================
-    // Two warps share each TMEM lane quadrant (one query row per lane); warp
-    // half `ch` owns half of the row's columns.  Partners exchange the row max
-    // (and, per group, the probability sum) through shared memory.
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
     const int ch = (warp - 2) >> 2;            // column half of this warp
     const int r = quad * 32 + lane;            // tile row == TMEM lane
@@ -378,9 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       xslot ^= 1u;
       return o;
     };
-    uint32_t qpk[DH / 2];  // this row's half of Q as packed bf16 pairs
     bool ok = mbar_wait_bounded(q_full, 0, kPollLimit);
     {  // copy this row's half of Q into TMEM, the A operand of the score MMAs
+      uint32_t qpk[DH / 2];
 #pragma unroll
       for (int x = 0; x < DH / 8; ++x) {
         const int d = ch * DH + x * 8, bx = d / 64, c = (d % 64) / 8;
@@ -417,30 +433,51 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       return true;
     };
 
-    for (int64_t n = 0; n < total && ok; ++n) {
-      const int b = int(n % 3);
-      if (!mbar_wait_bounded(&s_full[b], uint32_t((n / 3) & 1), kPollLimit)) { ok = false; break; }
+    // wait for the scores of step n; returns this thread's S-buffer address
+    auto wait_scores = [&](int64_t n, uint32_t& tS) -> bool {
+      const int b = int(n & 1);
+      if (!mbar_wait_bounded(&s_full[b], uint32_t((n >> 1) & 1), kPollLimit)) return false;
       if (lane == 0) PASA_TRACE_MARK(4 + (warp - 2), n);
       tc_fence_after();
-      const uint32_t tS = tmem + lane_base + C::kColS0 + 64u * b;
-      if (n < nU) {
-        // ---------------- Phase 1: exact block ----------------
-        const uint32_t e = ulist[n];  // (block << 2) | bit per half
-        const int64_t j = e >> 2;
-        const bool active = live && ((e >> half) & 1u);  // uniform per warp
-        uint32_t pk[16];
-        if (active) {
-          uint32_t sv[32];
-          tmem_ld16(tS + ch * 32 + 0, *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
-          tmem_ld16(tS + ch * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
-          tmem_wait_ld();
-          if (j == NT - 1) {  // key rows >= T are masked (:178); only the last block has them
-            const int nvalid = int(last_len) - ch * 32;
-#pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
+      tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(b);
+      return true;
+    };
+    // hand P (and U) of step n to the MMA warp
+    auto release_step = [&](int64_t n) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) PASA_TRACE_MARK(12 + (warp - 2), n);
+      if (lane == 0) mbar_arrive(&p_ready[n & 1]);
+    };
+
+    for (int64_t n = 0; n < nP && ok; ++n) {
+      uint32_t tS;
+      if (!wait_scores(n, tS)) { ok = false; break; }
+      {
+        // ---------------- Phase 1: a pair of exact blocks ----------------
+        // this thread owns columns [32 ch, 32 ch + 32) of each block
+        const uint32_t e0 = ulist[2 * n];
+        const uint32_t e1 = (2 * n + 1 < nU) ? uint32_t(ulist[2 * n + 1]) : 0u;  // lone last block: no bits
+        const bool act0 = live && ((e0 >> half) & 1u);  // uniform per warp
+        const bool act1 = live && ((e1 >> half) & 1u);
+        uint32_t pk0[16], pk1[16];
+        if (act0 || act1) {
+          uint32_t s0[32], s1[32];
+          if (act0) {
+            tmem_ld16(tS + ch * 32 + 0, *reinterpret_cast<uint32_t(*)[16]>(&s0[0]));
+            tmem_ld16(tS + ch * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&s0[16]));
           }
-          float mx = max_tree32(sv);
+          if (act1) {
+            tmem_ld16(tS + 64 + ch * 32 + 0, *reinterpret_cast<uint32_t(*)[16]>(&s1[0]));
+            tmem_ld16(tS + 64 + ch * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&s1[16]));
+          }
+          tmem_wait_ld();
+          // key rows >= T are masked (:178); only the last block has them
+          if (!act0) mask_tail32(s0, 0);
+          else if (int64_t(e0 >> 2) == NT - 1) mask_tail32(s0, int(last_len) - ch * 32);
+          if (!act1) mask_tail32(s1, 0);
+          else if (int64_t(e1 >> 2) == NT - 1) mask_tail32(s1, int(last_len) - ch * 32);
+          float mx = fmaxf(max_tree32(s0), max_tree32(s1));
           mx = fmaxf(mx, exchange(mx)) * sm_scale;  // max commutes with the positive scale
           m_true = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;
@@ -451,16 +488,42 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           }
           l1 *= alpha;
           if (grow) m_used = mx;
-          l1 += exp2_pack32(sv, sm_scale, -m_used, pk);
+          if (act0) {
+            l1 += exp2_pack32(s0, sm_scale, -m_used, pk0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) pk0[c] = 0u;
+          }
+          if (act1) {
+            l1 += exp2_pack32(s1, sm_scale, -m_used, pk1);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) pk1[c] = 0u;
+          }
         } else {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) pk[c] = 0u;
+          for (int c = 0; c < 16; ++c) { pk0[c] = 0u; pk1[c] = 0u; }
         }
-        tmem_st16(tS + ch * 16, pk);
+        tmem_st16(tS + ch * 16, pk0);       // keys [32 ch, 32 ch + 32) of block 0
+        tmem_st16(tS + 32 + ch * 16, pk1);  // keys [64 + 32 ch, ...) of block 1
         tmem_wait_st();
-      } else {
+      }
+      release_step(n);
+    }
+
+    uint32_t qpk[DH / 2];  // this row's half of Q (packed bf16), read back from TMEM for phase 2
+    if (ok) {
+#pragma unroll
+      for (int c0 = 0; c0 < DH / 2; c0 += 16)
+        tmem_ld16(tmem + lane_base + C::kColQ + ch * (DH / 2) + c0, *reinterpret_cast<uint32_t(*)[16]>(&qpk[c0]));
+      tmem_wait_ld();
+    }
+    for (int64_t n = nP; n < total && ok; ++n) {
+      uint32_t tS;
+      if (!wait_scores(n, tS)) { ok = false; break; }
+      {
         // ---------------- Phase 2: group g ----------------
-        const int64_t g = n - nU;
+        const int64_t g = n - nP;
         uint32_t pk[8];
         uint32_t upk[DH / 2];
         if (live) {
@@ -518,16 +581,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           for (int x = 0; x < DH / 2; ++x) upk[x] = 0u;
         }
         tmem_st8(tS + ch * 8, pk);
-        const uint32_t tU = tmem + lane_base + C::kColU0 + 64u * uint32_t(n & 1) + ch * (DH / 2);
+        const uint32_t tU = tS + C::kColU + ch * (DH / 2);
 #pragma unroll
         for (int c0 = 0; c0 < DH / 2; c0 += 16)
           tmem_st16(tU + c0, *reinterpret_cast<uint32_t(*)[16]>(&upk[c0]));
         tmem_wait_st();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) PASA_TRACE_MARK(12 + (warp - 2), n);
-      if (lane == 0) mbar_arrive(&p_ready[b]);
+      release_step(n);
     }
 
     // ---------------- Final: o = O / (l + g_l) ----------------

@@ -274,40 +274,27 @@ __device__ __forceinline__ float max_tree16(const uint32_t (&v)[16]) {
   return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]));
 }
 
-// Packed fp32 pair arithmetic (sm_100): d = a * b + c and d = a + b, lane-wise.
-__device__ __forceinline__ void fma_f32x2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
-                                          float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-__device__ __forceinline__ void add_f32x2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi);
 
 // p_c = 2^(s_c * scale + negm) for 32 raw fp32 scores; packs bf16 pairs into
-// pk and returns the fp32 sum of the p_c.
+// pk and returns the fp32 sum of the p_c.  The scale/shift and the sums use
+// the sm_100 packed fp32 pair instructions.
 __device__ __forceinline__ float exp2_pack32(const uint32_t (&sv)[32], float scale, float negm,
                                              uint32_t (&pk)[16]) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  const float2 sc = make_float2(scale, scale), nm = make_float2(negm, negm);
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < 32; c += 4) {
-    float x0, x1, x2, x3;
-    fma_f32x2(x0, x1, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), scale, scale, negm, negm);
-    fma_f32x2(x2, x3, __uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]), scale, scale, negm, negm);
-    x0 = fast_exp2(x0); x1 = fast_exp2(x1); x2 = fast_exp2(x2); x3 = fast_exp2(x3);
-    pk[c / 2] = pack_bf16x2(x0, x1);
-    pk[c / 2 + 1] = pack_bf16x2(x2, x3);
-    add_f32x2(s0, s1, s0, s1, x0, x1);
-    add_f32x2(s2, s3, s2, s3, x2, x3);
+    float2 x01 = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc, nm);
+    float2 x23 = __ffma2_rn(make_float2(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3])), sc, nm);
+    x01.x = fast_exp2(x01.x); x01.y = fast_exp2(x01.y);
+    x23.x = fast_exp2(x23.x); x23.y = fast_exp2(x23.y);
+    pk[c / 2] = pack_bf16x2(x01.x, x01.y);
+    pk[c / 2 + 1] = pack_bf16x2(x23.x, x23.y);
+    acc0 = __fadd2_rn(acc0, x01);
+    acc1 = __fadd2_rn(acc1, x23);
   }
-  return (s0 + s1) + (s2 + s3);
+  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

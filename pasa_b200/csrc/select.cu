@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   uint64_t* compact = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(maskw + kRows * NG) + 7) & ~uintptr_t(7));
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t bh = blockIdx.y;
   const int64_t i0 = int64_t(blockIdx.x) * kRows;
   const int nrows = int((NT - i0 < kRows) ? (NT - i0) : int64_t(kRows));
