@@ -12,9 +12,10 @@
 // B200 mapping:
 //   * a CTA owns a PAIR of adjacent 64-query blocks (128 rows), so every MMA
 //     is M=128 (the full tcgen05 datapath).  Phase 1 walks the union of the
-//     two blocks' selected key blocks in ascending order, TWO key blocks per
-//     step: the score MMA is N=128 (full rate; N=64 runs at ~55%) and P.V is
-//     K=128.  Rows whose query block did not select a key block get P = 0
+//     two blocks' selected key blocks, TWO key blocks per step: the score MMA
+//     is N=128 (full rate; N=64 runs at ~55%) and P.V is K=128.  Steps pair a
+//     block only query block A selected with one only B selected where
+//     possible, so both halves of the softmax carry equal work.  Rows whose query block did not select a key block get P = 0
 //     and skip its exponentials.  Phase 2 (shared by both query blocks) walks
 //     the 32-block groups with each half's own selection bits.
 //   * Q lives in TMEM as the A operand of every score MMA, so shared memory
@@ -178,30 +179,64 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     maskw[kMaxNG + w] = hasB ? P.sel_mask[(bh * NT + blkB) * NG + w] : 0u;
   }
   __syncthreads();
-  if (warp == 0) {  // union of the two selections, ascending block index
-    uint32_t base = 0;
+  if (warp == 0) {
+    // Union of the two selections, ordered so that consecutive pairs (one
+    // phase-1 step) balance the two halves: blocks only A selected alternate
+    // with blocks only B selected, then the leftover single-half blocks, then
+    // the blocks both selected.  Within each category the order is ascending.
+    // (The softmax is order-independent, so any order gives the same result
+    // up to floating-point rounding.)
+    uint32_t na = 0, nb = 0, nboth = 0;
     for (int64_t w0 = 0; w0 < NG; w0 += 32) {
       const int64_t w = w0 + lane;
       const uint32_t ma = (w < NG) ? maskw[w] : 0u, mb = (w < NG) ? maskw[kMaxNG + w] : 0u;
-      const uint32_t u = ma | mb;
-      const uint32_t cnt = __popc(u);
-      uint32_t incl = cnt;
+      na += __popc(ma & ~mb); nb += __popc(mb & ~ma); nboth += __popc(ma & mb);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      na += __shfl_xor_sync(0xffffffffu, na, off);
+      nb += __shfl_xor_sync(0xffffffffu, nb, off);
+      nboth += __shfl_xor_sync(0xffffffffu, nboth, off);
+    }
+    const uint32_t m = na < nb ? na : nb;
+    uint32_t ka = 0, kb = 0, kab = 0;  // running counts per category
+    for (int64_t w0 = 0; w0 < NG; w0 += 32) {
+      const int64_t w = w0 + lane;
+      const uint32_t ma = (w < NG) ? maskw[w] : 0u, mb = (w < NG) ? maskw[kMaxNG + w] : 0u;
+      const uint32_t ua = ma & ~mb, ub = mb & ~ma, uab = ma & mb;
+      uint32_t ca = __popc(ua), cb = __popc(ub), cab = __popc(uab);
+      uint32_t ia = ca, ib = cb, iab = cab;  // inclusive scans over lanes
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
+        const uint32_t ya = __shfl_up_sync(0xffffffffu, ia, off);
+        const uint32_t yb = __shfl_up_sync(0xffffffffu, ib, off);
+        const uint32_t yab = __shfl_up_sync(0xffffffffu, iab, off);
+        if (lane >= off) { ia += ya; ib += yb; iab += yab; }
       }
-      uint32_t pos = base + incl - cnt;
-      uint32_t rem = u;
-      while (rem) {
-        const int b = __ffs(rem) - 1;
-        rem &= rem - 1;
-        const uint32_t j = uint32_t(w * 32 + b);
-        ulist[pos++] = uint16_t((j << 2) | ((ma >> b) & 1u) | (((mb >> b) & 1u) << 1));
+      uint32_t pa = ka + ia - ca, pb = kb + ib - cb, pab = kab + iab - cab;  // category ranks
+      for (uint32_t rem = ua | ub | uab; rem; rem &= rem - 1) {
+        const int bit = __ffs(rem) - 1;
+        const uint32_t j = uint32_t(w * 32 + bit);
+        uint32_t pos;
+        if ((ua >> bit) & 1u) {
+          pos = (pa < m) ? 2 * pa : 2 * m + (pa - m);
+          ++pa;
+          ulist[pos] = uint16_t((j << 2) | 1u);
+        } else if ((ub >> bit) & 1u) {
+          pos = (pb < m) ? 2 * pb + 1 : 2 * m + (na - m) + (pb - m);
+          ++pb;
+          ulist[pos] = uint16_t((j << 2) | 2u);
+        } else {
+          pos = na + nb + pab;
+          ++pab;
+          ulist[pos] = uint16_t((j << 2) | 3u);
+        }
       }
-      base += __shfl_sync(0xffffffffu, incl, 31);
+      ka += __shfl_sync(0xffffffffu, ia, 31);
+      kb += __shfl_sync(0xffffffffu, ib, 31);
+      kab += __shfl_sync(0xffffffffu, iab, 31);
     }
-    if (lane == 0) s_nu = base;
+    if (lane == 0) s_nu = na + nb + nboth;
   }
   tc_fence_before();
   __syncthreads();
