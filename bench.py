@@ -174,21 +174,16 @@ def init_dist():
 
 
 def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from pasa_b200 import dist as pdist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return pdist.max_over_ranks(x) if world > 1 else x
 
 
 def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
+    from pasa_b200 import dist as pdist
 
-        dist.barrier()
+    if world > 1:
+        pdist.barrier()
 
 
 def run_reference(args):
