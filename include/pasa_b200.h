@@ -139,6 +139,32 @@ PASA_API int pasa_forward(void* stream, const void* q, const void* k, const void
                  void* workspace, size_t workspace_bytes, void* o, int kernel);
 
 /*
+ * The whole op like pasa_forward, but with no workspace argument and no
+ * allocation anywhere: the scratch (block statistics, top-k indices,
+ * selection bitmask, error word) is a 32 MiB array built into this library,
+ * which every GPU that loads the library holds until the process exits.
+ * This entry point has no counterpart in the reference.  It is meant for
+ * callers that cannot call cudaMalloc: hosts that own all device memory
+ * through their own pool, plugin interfaces that pass no allocator, and
+ * latency-critical paths where an allocation's implicit synchronisation is
+ * not acceptable.
+ *   - Problems whose scratch (pasa_workspace_size) exceeds 32 MiB return
+ *     PASA_ERR_WORKSPACE without launching anything.  At D=128, bf16 and
+ *     density 0.1 that allows about 11 heads of 75600 tokens per call.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress) and caches it.  Make that first call before
+ *     any stream capture.
+ *   - Every call on a device shares the one array, which keeps the last
+ *     call's contents.  Calls whose work overlaps on the GPU (for example on
+ *     two streams at once) race on it and must be serialised by the caller.
+ * Arguments and results are those of pasa_forward.
+ */
+PASA_API int pasa_forward_noalloc(void* stream, const void* q, const void* k, const void* v,
+                 int64_t B, int64_t H, int64_t T, int D, int dtype,
+                 double density, float scale, int use_cov_bias, const float* noise,
+                 void* o, int kernel);
+
+/*
  * Token-layout permutation of the temporal heads (frame-major <-> token-
  * major), text tail untouched.  Replaces hunyuan_sparse_head_placement
  * (svg/models/hyvideo/placement.py:34-153) when inverse = 0 and

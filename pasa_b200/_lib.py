@@ -35,7 +35,7 @@ DEVERR_WAIT_TIMEOUT = 0x1
 
 EXPORTS = (
     "pasa_abi_version", "pasa_status_string", "pasa_derive", "pasa_workspace_size", "pasa_prep",
-    "pasa_select", "pasa_attn", "pasa_forward", "pasa_place",
+    "pasa_select", "pasa_attn", "pasa_forward", "pasa_forward_noalloc", "pasa_place",
 )
 
 _lib = None
@@ -66,6 +66,8 @@ def load() -> ctypes.CDLL:
                                  P, P, c_size_t, P, c_int]),
         "pasa_place": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int64,
                                c_int]),
+        "pasa_forward_noalloc": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float,
+                                         c_int, P, P, c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
