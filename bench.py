@@ -331,6 +331,9 @@ def main():
     F_rank = w.exact_flops(nh)
     achieved = F_rank / (attn_ms * 1e-3) / 1e12
     traffic = ATTN_TRAFFIC_BYTES.get((w.name, args.kernel if args.kernel != "auto" else "tcgen05"))
+    if traffic is not None:
+        full = synth.WORKLOADS[args.config].heads
+        traffic = traffic * nh / full  # this rank's launch covers nh of the workload's heads
     roofline = {
         "kernel": "attn_tc_kernel<128>" if kernel != _lib.ATTN_SIMT else "attn_simt_kernel",
         "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
