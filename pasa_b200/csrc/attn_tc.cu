@@ -112,7 +112,7 @@ struct Params {
 // pasa_trace_read() copies them out.
 #ifdef PASA_TRACE
 constexpr int kTraceSteps = 1024;
-__device__ unsigned long long g_pasa_trace[24][kTraceSteps];
+__device__ unsigned long long g_pasa_trace[28][kTraceSteps];
 #define PASA_TRACE_MARK(ev, step)                                                        \
   do {                                                                                    \
     if (blockIdx.x == 0 && blockIdx.y == 0 && (step) < kTraceSteps)                       \
@@ -439,9 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                                                        ((c ^ (r & 7)) << 4));
         qpk[x * 4 + 0] = v.x; qpk[x * 4 + 1] = v.y; qpk[x * 4 + 2] = v.z; qpk[x * 4 + 3] = v.w;
       }
-#pragma unroll
-      for (int c0 = 0; c0 < DH / 2; c0 += 16)
-        tmem_st16(tmem + lane_base + C::kColQ + ch * (DH / 2) + c0, *reinterpret_cast<uint32_t(*)[16]>(&qpk[c0]));
+      tmem_st<DH / 2>(tmem + lane_base + C::kColQ + ch * (DH / 2), qpk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -498,22 +496,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         uint32_t pk0[16], pk1[16];
         if (act0 || act1) {
           uint32_t s0[32], s1[32];
-          if (act0) {
-            tmem_ld16(tS + ch * 32 + 0, *reinterpret_cast<uint32_t(*)[16]>(&s0[0]));
-            tmem_ld16(tS + ch * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&s0[16]));
-          }
-          if (act1) {
-            tmem_ld16(tS + 64 + ch * 32 + 0, *reinterpret_cast<uint32_t(*)[16]>(&s1[0]));
-            tmem_ld16(tS + 64 + ch * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&s1[16]));
-          }
+          if (act0) tmem_ld32(tS + ch * 32, s0);
+          if (act1) tmem_ld32(tS + 64 + ch * 32, s1);
           tmem_wait_ld();
+#ifdef PASA_TRACE
+          if (warp == 2) {  // trace only: force the loaded registers to be consumed before stamping
+            uint32_t x = (act0 ? s0[0] ^ s0[31] : 0u) ^ (act1 ? s1[0] ^ s1[31] : 0u);
+            asm volatile("" : "+r"(x));
+            if (x == 0x7fffffffu && lane == 33) PASA_TRACE_MARK(27, n);
+          }
+#endif
+          if (warp == 2 && lane == 0) PASA_TRACE_MARK(24, n);
           // key rows >= T are masked (:178); only the last block has them
-          if (!act0) mask_tail32(s0, 0);
-          else if (int64_t(e0 >> 2) == NT - 1) mask_tail32(s0, int(last_len) - ch * 32);
-          if (!act1) mask_tail32(s1, 0);
-          else if (int64_t(e1 >> 2) == NT - 1) mask_tail32(s1, int(last_len) - ch * 32);
-          float mx = fmaxf(max_tree32(s0), max_tree32(s1));
+          if (act0 && int64_t(e0 >> 2) == NT - 1) mask_tail32(s0, int(last_len) - ch * 32);
+          if (act1 && int64_t(e1 >> 2) == NT - 1) mask_tail32(s1, int(last_len) - ch * 32);
+          float mx = -INFINITY;
+          if (act0) mx = max_tree32(s0);
+          if (act1) mx = fmaxf(mx, max_tree32(s1));
+          if (warp == 2 && lane == 0) PASA_TRACE_MARK(25, n);
           mx = fmaxf(mx, exchange(mx)) * sm_scale;  // max commutes with the positive scale
+          if (warp == 2 && lane == 0) PASA_TRACE_MARK(26, n);
           m_true = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;
           const bool need = grow && (m_used != -INFINITY);
@@ -539,6 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
           for (int c = 0; c < 16; ++c) { pk0[c] = 0u; pk1[c] = 0u; }
         }
+        if (warp == 2 && lane == 0) PASA_TRACE_MARK(27, n);
         tmem_st16(tS + ch * 16, pk0);       // keys [32 ch, 32 ch + 32) of block 0
         tmem_st16(tS + 32 + ch * 16, pk1);  // keys [64 + 32 ch, ...) of block 1
         tmem_wait_st();
@@ -548,9 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 
     uint32_t qpk[DH / 2];  // this row's half of Q (packed bf16), read back from TMEM for phase 2
     if (ok) {
-#pragma unroll
-      for (int c0 = 0; c0 < DH / 2; c0 += 16)
-        tmem_ld16(tmem + lane_base + C::kColQ + ch * (DH / 2) + c0, *reinterpret_cast<uint32_t(*)[16]>(&qpk[c0]));
+      tmem_ld<DH / 2>(tmem + lane_base + C::kColQ + ch * (DH / 2), qpk);
       tmem_wait_ld();
     }
     for (int64_t n = nP; n < total && ok; ++n) {
@@ -589,13 +590,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           for (int c = 0; c < 16; ++c) p[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
           float psum = 0.f, wsum;
           {
-            float a0 = 0.f, a1 = 0.f;
+            float a0 = 0.f, a1 = 0.f, extra = 0.f;
+            const int64_t last_rel = NT - 1 - jb0;  // column of the ragged last block, if in range
 #pragma unroll
-            for (int c = 0; c < 16; c += 2) { a0 += p[c]; a1 += p[c + 1]; }
+            for (int c = 0; c < 16; c += 2) {
+              a0 += p[c]; a1 += p[c + 1];
+              extra += (c == last_rel) ? p[c] : ((c + 1 == last_rel) ? p[c + 1] : 0.f);
+            }
             psum = a0 + a1;
-            wsum = psum * float(kBlock);
-            if (jb0 <= NT - 1 && NT - 1 < jb0 + 16)  // the ragged last block has its own length (:220)
-              wsum += p[NT - 1 - jb0] * float(last_len - kBlock);
+            // the ragged last block has its own length (:220)
+            wsum = psum * float(kBlock) + extra * float(last_len - kBlock);
           }
 #pragma unroll
           for (int c = 0; c < 16; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
@@ -616,10 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           for (int x = 0; x < DH / 2; ++x) upk[x] = 0u;
         }
         tmem_st8(tS + ch * 8, pk);
-        const uint32_t tU = tS + C::kColU + ch * (DH / 2);
-#pragma unroll
-        for (int c0 = 0; c0 < DH / 2; c0 += 16)
-          tmem_st16(tU + c0, *reinterpret_cast<uint32_t(*)[16]>(&upk[c0]));
+        tmem_st<DH / 2>(tS + C::kColU + ch * (DH / 2), upk);
         tmem_wait_st();
       }
       release_step(n);
