@@ -23,14 +23,18 @@
 //     core reads them once.
 //   * warp 0: TMA producer (ring 1: K/V of block pairs, 3 slots; ring 2,
 //     aliased on the same memory: kc/vc rows and H of a group); warp 1: TMEM
-//     owner and MMA issuer (one thread, non-blocking event loop); warps 2-9:
+//     owner and score-MMA issuer; warp 2: P.V / correction MMA issuer (one
+//     thread issues a tcgen05.mma only every ~90 cycles, so a single issuer
+//     would cap the tensor core at ~70% for these shapes); warps 3-10:
 //     softmax, two threads per query row (TMEM lane), each owning half of
-//     every key block's columns; partner warps exchange row maxima and
-//     probability sums through shared memory.
-//   * TMEM: O (fp32), Q (bf16), two S buffers of 128 columns.  P is written
-//     back over S as packed bf16; in phase 2 the first-order operand
-//     U = bf16(w_t q_t) (w_t = scale * sum of the group's probabilities) sits
-//     in the S buffer's upper half and U.H_g is accumulated straight into O.
+//     every key block's columns; the two warps of a lane quadrant
+//     combine row maxima and probability sums through shared memory.
+//   * TMEM: O (fp32), Q (bf16), P (bf16) and two S buffers of 128 columns.
+//     The softmax frees an S buffer as soon as its scores are in registers,
+//     so the score MMAs of step n+2 overlap the softmax and P.V of step n.
+//     In phase 2 the first-order operand U = bf16(w_t q_t) (w_t = scale *
+//     sum of the group's probabilities) sits in the S buffer's upper half and
+//     U.H_g is accumulated straight into O.
 //   * softmax rescales O only when a row max grows by more than 2^8
 //     (exact either way: O and l share the stale max); the exact running max
 //     is tracked separately to reproduce g_l.
@@ -45,7 +49,9 @@ namespace pasa {
 
 namespace tc {
 
-constexpr int kThreads = 320;          // 10 warps: TMA, MMA, 8 softmax
+constexpr int kParts = 2;              // softmax threads per query row
+constexpr int kSoftmaxWarps = 4 * kParts;
+constexpr int kThreads = 32 * (3 + kSoftmaxWarps);  // TMA, S issuer, P.V issuer, softmax
 constexpr int kRowsPerTile = 128;      // two query blocks
 constexpr float kRescaleThresh = 8.0f; // log2 units
 constexpr int kMaxNT = 4096;           // union list capacity (entries)
@@ -73,7 +79,8 @@ struct Cfg {
   // TMEM columns
   static constexpr uint32_t kColO = 0;
   static constexpr uint32_t kColQ = 128;
-  static constexpr uint32_t kColS0 = 192;               // S buffer b at kColS0 + 128 b
+  static constexpr uint32_t kColP = 192;                // P (packed bf16) of the step in flight
+  static constexpr uint32_t kColS0 = 256;               // S buffer b at kColS0 + 128 b
   static constexpr uint32_t kColU = 64;                 // phase 2: U inside the S buffer
   static constexpr uint32_t kTmemCols = 512;
   // shared memory carve-up (offsets from a 1024-aligned base).  Q is staged
@@ -82,9 +89,9 @@ struct Cfg {
   static constexpr int kOffQ = 2 * kSlot1;
   static constexpr int kOffUnion = kOffRing + kRingBytes;            // u16 [kMaxNT]
   static constexpr int kOffMask = kOffUnion + kMaxNT * 2;            // u32 [2][kMaxNG]
-  static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][2 halves][128]
-  static constexpr int kOffBar = kOffXch + 2 * 2 * kRowsPerTile * 4;
-  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 2 + 2 + 2 + 2;
+  static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][kParts][128]
+  static constexpr int kOffBar = kOffXch + 2 * kParts * kRowsPerTile * 4;
+  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 2 + 2 + 2 + 2 + 2;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
   static_assert(kOffQ + kQBytes <= kRingBytes, "Q staging must fit in the ring");
@@ -112,7 +119,7 @@ struct Params {
 // pasa_trace_read() copies them out.
 #ifdef PASA_TRACE
 constexpr int kTraceSteps = 1024;
-__device__ unsigned long long g_pasa_trace[28][kTraceSteps];
+__device__ unsigned long long g_pasa_trace[30][kTraceSteps];
 #define PASA_TRACE_MARK(ev, step)                                                        \
   do {                                                                                    \
     if (blockIdx.x == 0 && blockIdx.y == 0 && (step) < kTraceSteps)                       \
@@ -127,9 +134,10 @@ __device__ __forceinline__ void report(uint32_t* err) {
 }
 
 // Set the raw fp32 scores of columns c >= nvalid to -inf.
-__device__ __forceinline__ void mask_tail32(uint32_t (&sv)[32], int nvalid) {
+template <int N>
+__device__ __forceinline__ void mask_tail(uint32_t (&sv)[N], int nvalid) {
 #pragma unroll
-  for (int c = 0; c < 32; ++c)
+  for (int c = 0; c < N; ++c)
     if (c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
 }
 
@@ -151,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* s_full = q_tmem + 1;   // [2]
   uint64_t* p_ready = s_full + 2;  // [2]
   uint64_t* o_done = p_ready + 2;  // [2]
+  uint64_t* s_free = o_done + 2;   // [2] phase-1 scores of the buffer are in registers
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffSlot);
   __shared__ uint32_t s_nu;
 
@@ -165,8 +174,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     for (int s = 0; s < C::kS1; ++s) { mbar_init(&full1[s], 1); mbar_init(&empty1[s], 1); }
     for (int s = 0; s < C::kS2; ++s) { mbar_init(&full2[s], 1); mbar_init(&empty2[s], 1); }
     mbar_init(q_full, 1);
-    mbar_init(q_tmem, 8);
-    for (int b = 0; b < 2; ++b) { mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], 8); mbar_init(&o_done[b], 1); }
+    mbar_init(q_tmem, kSoftmaxWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], kSoftmaxWarps); mbar_init(&o_done[b], 1);
+      mbar_init(&s_free[b], kSoftmaxWarps);
+    }
     fence_barrier_init();
   }
   if (warp == 1) { tmem_alloc(tmem_slot, C::kTmemCols); tmem_relinquish(); }
@@ -311,8 +323,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         else mbar_wait_bounded(&full2[(n - nP) % C::kS2], uint32_t(((n - nP) / C::kS2) & 1), kPollLimit);
       }
     }
-  } else if (warp == 1) {
-    // ================= MMA issuer =================
+  } else if (warp == 1 || warp == 2) {
+    // ================= MMA issuers =================
+    // One thread can issue a tcgen05.mma only every ~90 cycles, slower than
+    // the tensor core retires an M128 N128 K16 step, so the score MMAs
+    // (warp 1) and the P.V / correction MMAs (warp 2) have an issuer each.
+    // Their only shared resource is the S buffer: S(n) may overwrite buffer
+    // n & 1 once the softmax has pulled the phase-1 scores of step n-2 into
+    // registers (s_free), or, for a phase-2 step n-2, once its P.V, which
+    // reads U from that buffer, has completed (o_done).
     if (lane == 0) {
       constexpr uint32_t idS128 = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idS32 = umma_idesc_bf16(128, 32, false, false);
@@ -325,121 +344,120 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         return (n < nP) ? smem_u32(sm + C::kOffRing + int(n % C::kS1) * C::kSlot1)
                         : smem_u32(sm + C::kOffRing + int((n - nP) % C::kS2) * C::kSlot2);
       };
-      auto data_ready = [&](int64_t n) -> bool {
-        if (n < nP) return mbar_test(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1));
-        const int64_t g = n - nP;
-        return mbar_test(&full2[g % C::kS2], uint32_t((g / C::kS2) & 1));
-      };
-      auto issue_s = [&](int64_t n) {
-        PASA_TRACE_MARK(1, n);
-        tc_fence_after();
-        const uint32_t st = slot_addr(n);
-        const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(n & 1);
-        if (n < nP) {  // S = Q . [K_j0; K_j1]^T, N = 128
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int bx = kk / 4, ko = (kk % 4) * 32;
-            const uint64_t bd = umma_desc_sw128(st + bx * C::kPairBox + ko, 16, 1024);
-            mma_ts(tS, tQ + kk * 8, bd, idS128, kk > 0 ? 1u : 0u);
+      if (warp == 1) {
+        for (int64_t n = 0; n < total && ok; ++n) {
+          if (n >= 2) {
+            const int64_t m = n - 2;
+            const bool freed = (m < nP) ? mbar_wait_bounded(&s_free[m & 1], uint32_t((m >> 1) & 1), kPollLimit)
+                                        : mbar_wait_bounded(&o_done[m & 1], uint32_t((m >> 1) & 1), kPollLimit);
+            if (!freed) { ok = false; break; }
           }
-        } else {       // S = Q . kc_g^T, N = 32
+          const bool landed = (n < nP)
+              ? mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)
+              : mbar_wait_bounded(&full2[(n - nP) % C::kS2], uint32_t(((n - nP) / C::kS2) & 1), kPollLimit);
+          if (!landed) { ok = false; break; }
+          PASA_TRACE_MARK(1, n);
+          tc_fence_after();
+          const uint32_t st = slot_addr(n);
+          const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(n & 1);
+          if (n < nP) {  // S = Q . [K_j0; K_j1]^T, N = 128
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int bx = kk / 4, ko = (kk % 4) * 32;
-            const uint64_t bd = umma_desc_sw128(st + bx * (kGroup * 128) + ko, 16, 1024);
-            mma_ts(tS, tQ + kk * 8, bd, idS32, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int bx = kk / 4, ko = (kk % 4) * 32;
+              const uint64_t bd = umma_desc_sw128(st + bx * C::kPairBox + ko, 16, 1024);
+              mma_ts(tS, tQ + kk * 8, bd, idS128, kk > 0 ? 1u : 0u);
+            }
+          } else {       // S = Q . kc_g^T, N = 32
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int bx = kk / 4, ko = (kk % 4) * 32;
+              const uint64_t bd = umma_desc_sw128(st + bx * (kGroup * 128) + ko, 16, 1024);
+              mma_ts(tS, tQ + kk * 8, bd, idS32, kk > 0 ? 1u : 0u);
+            }
           }
+          PASA_TRACE_MARK(28, n);
+          tc_commit(&s_full[n & 1]);
         }
-        tc_commit(&s_full[n & 1]);
-      };
-      auto issue_pv = [&](int64_t m) {
-        PASA_TRACE_MARK(2, m);
-        tc_fence_after();
-        const uint32_t st = slot_addr(m);
-        const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(m & 1);
-        if (m < nP) {  // O += P . [V_j0; V_j1], K = 128
+      } else {
+        for (int64_t m = 0; m < total && ok; ++m) {
+          if (!mbar_wait_bounded(&p_ready[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) { ok = false; break; }
+          PASA_TRACE_MARK(2, m);
+          tc_fence_after();
+          const uint32_t st = slot_addr(m);
+          const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(m & 1);
+          if (m < nP) {  // O += P . [V_j0; V_j1], K = 128
 #pragma unroll
-          for (int kk = 0; kk < 2 * kBlock / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(st + 2 * C::kKVBytes + kk * 2048, C::kPairBox, 1024);
-            mma_ts(tmem + C::kColO, tS + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&empty1[m % C::kS1]);
-        } else {       // O += P_g . vc_g + U_g . H_g
+            for (int kk = 0; kk < 2 * kBlock / 16; ++kk) {
+              const uint64_t bd = umma_desc_sw128(st + 2 * C::kKVBytes + kk * 2048, C::kPairBox, 1024);
+              mma_ts(tmem + C::kColO, tmem + C::kColP + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit(&empty1[m % C::kS1]);
+          } else {       // O += P_g . vc_g + U_g . H_g
 #pragma unroll
-          for (int kk = 0; kk < kGroup / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(st + C::kCBytes + kk * 2048, C::kCBytes / C::kBoxes, 1024);
-            mma_ts(tmem + C::kColO, tS + kk * 8, bd, idPV, 1u);
-          }
+            for (int kk = 0; kk < kGroup / 16; ++kk) {
+              const uint64_t bd = umma_desc_sw128(st + C::kCBytes + kk * 2048, C::kCBytes / C::kBoxes, 1024);
+              mma_ts(tmem + C::kColO, tmem + C::kColP + kk * 8, bd, idPV, 1u);
+            }
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(st + 2 * C::kCBytes + kk * 2048, C::kHBytes / C::kBoxes, 1024);
-            mma_ts(tmem + C::kColO, tS + C::kColU + kk * 8, bd, idPV, 1u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t bd = umma_desc_sw128(st + 2 * C::kCBytes + kk * 2048, C::kHBytes / C::kBoxes, 1024);
+              mma_ts(tmem + C::kColO, tS + C::kColU + kk * 8, bd, idPV, 1u);
+            }
+            tc_commit(&empty2[(m - nP) % C::kS2]);
           }
-          tc_commit(&empty2[(m - nP) % C::kS2]);
-        }
-        tc_commit(&o_done[m & 1]);
-      };
-
-      // Event loop: issue whichever of the next S (needs its TMA data) or the
-      // next P.V (needs the softmax) is ready.  S runs at most one step ahead
-      // of P.V (two S buffers).  Ring 2 reuses ring 1's memory, so group
-      // scores wait until every phase-1 P.V is issued.
-      int64_t ns = 0, npv = 0;
-      uint64_t idle_since = 0;
-      while (ok && npv < total) {
-        bool progressed = false;
-        if (npv < ns && mbar_test(&p_ready[npv & 1], uint32_t((npv >> 1) & 1))) {
-          issue_pv(npv++);
-          progressed = true;
-        }
-        if (ns < total && ns <= npv + 1 && (ns < nP || npv >= nP) && data_ready(ns)) {
-          issue_s(ns++);
-          progressed = true;
-        }
-        if (progressed) {
-          idle_since = 0;
-        } else {
-          __nanosleep(32);  // this warp shares its SM sub-partition with two softmax warps
-          if (idle_since == 0) idle_since = sm_cycles();
-          else if (sm_cycles() - idle_since > kPollLimit) ok = false;
+          tc_commit(&o_done[m & 1]);
+          PASA_TRACE_MARK(29, m);
         }
       }
       if (!ok) report(P.err);
     }
     __syncwarp();
   } else {
-    // ================= softmax / correction (warps 2..9) =================
+    // ================= softmax / correction (warps 3 .. 3 + kSoftmaxWarps) =================
+    // kParts threads per query row (TMEM lane): thread `part` owns columns
+    // [kPC part, kPC part + kPC) of both key blocks of a phase-1 step,
+    // columns [kGC part, kGC part + kGC) of a phase-2 group, and output
+    // columns [DQ part, DQ part + DQ).  The kParts warps of a lane quadrant combine
+    // row maxima and sums through shared memory.
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
-    const int ch = (warp - 2) >> 2;            // column half of this warp
+    const int part = (warp - 3) >> 2;          // column part of this warp
     const int r = quad * 32 + lane;            // tile row == TMEM lane
     const int half = r >> 6;                   // 0: block A, 1: block B
     const bool live = (half == 0) || hasB;     // uniform per warp
-    const int bar_id = 1 + quad;               // named barrier of the two partner warps
+    const int bar_id = 1 + quad;               // named barrier of the quadrant's kParts warps
     const uint32_t lane_base = uint32_t(quad * 32) << 16;
     const float scale32 = P.scale;
     const float sm_scale = scale32 * kLog2e;
     const int64_t last_len = P.T - (NT - 1) * kBlock;
-    constexpr int DH = D / 2;                  // output columns per partner
+    constexpr int DQ = D / kParts;             // Q / output columns per thread
+    constexpr int kPC = kBlock / kParts;       // score columns per key block per thread
+    constexpr int kGC = kGroup / kParts;       // group columns per thread
     float m_true = -INFINITY, m_used = -INFINITY, l1 = 0.f, gl = 0.f;
     uint32_t xslot = 0;
-    auto exchange = [&](float v) -> float {
-      xch[(xslot * 2 + ch) * kRowsPerTile + r] = v;
-      named_bar_sync(bar_id, 64);
-      const float o = xch[(xslot * 2 + (ch ^ 1)) * kRowsPerTile + r];
+    // combine one value per thread across the row's kParts threads (fixed order)
+    auto row_reduce = [&](float v, bool is_max) -> float {
+      xch[(xslot * kParts + part) * kRowsPerTile + r] = v;
+      named_bar_sync(bar_id, 32 * kParts);
+      float o = xch[(xslot * kParts) * kRowsPerTile + r];
+#pragma unroll
+      for (int q2 = 1; q2 < kParts; ++q2) {
+        const float x = xch[(xslot * kParts + q2) * kRowsPerTile + r];
+        o = is_max ? fmaxf(o, x) : o + x;
+      }
       xslot ^= 1u;
       return o;
     };
     bool ok = mbar_wait_bounded(q_full, 0, kPollLimit);
-    {  // copy this row's half of Q into TMEM, the A operand of the score MMAs
-      uint32_t qpk[DH / 2];
+    {  // copy this row's part of Q into TMEM, the A operand of the score MMAs
+      uint32_t qpk[DQ / 2];
 #pragma unroll
-      for (int x = 0; x < DH / 8; ++x) {
-        const int d = ch * DH + x * 8, bx = d / 64, c = (d % 64) / 8;
+      for (int x = 0; x < DQ / 8; ++x) {
+        const int d = part * DQ + x * 8, bx = d / 64, c = (d % 64) / 8;
         const uint4 v = *reinterpret_cast<const uint4*>(sm + C::kOffQ + bx * (kRowsPerTile * 128) + r * 128 +
                                                        ((c ^ (r & 7)) << 4));
         qpk[x * 4 + 0] = v.x; qpk[x * 4 + 1] = v.y; qpk[x * 4 + 2] = v.z; qpk[x * 4 + 3] = v.w;
       }
-      tmem_st<DH / 2>(tmem + lane_base + C::kColQ + ch * (DH / 2), qpk);
+      tmem_st<DQ / 2>(tmem + lane_base + C::kColQ + part * (DQ / 2), qpk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -454,13 +472,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         tc_fence_after();
       }
 #pragma unroll
-      for (int c0 = 0; c0 < DH; c0 += 16) {
+      for (int c0 = 0; c0 < DQ; c0 += 16) {
         uint32_t v[16];
-        tmem_ld16(tmem + lane_base + C::kColO + ch * DH + c0, v);
+        tmem_ld16(tmem + lane_base + C::kColO + part * DQ + c0, v);
         tmem_wait_ld();
 #pragma unroll
         for (int x = 0; x < 16; ++x) v[x] = __float_as_uint(__uint_as_float(v[x]) * alpha);
-        tmem_st16(tmem + lane_base + C::kColO + ch * DH + c0, v);
+        tmem_st16(tmem + lane_base + C::kColO + part * DQ + c0, v);
       }
       tmem_wait_st();
       return true;
@@ -470,16 +488,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     auto wait_scores = [&](int64_t n, uint32_t& tS) -> bool {
       const int b = int(n & 1);
       if (!mbar_wait_bounded(&s_full[b], uint32_t((n >> 1) & 1), kPollLimit)) return false;
-      if (lane == 0) PASA_TRACE_MARK(4 + (warp - 2), n);
+      if (lane == 0 && warp < 11) PASA_TRACE_MARK(4 + (warp - 3), n);
       tc_fence_after();
       tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(b);
+      return true;
+    };
+    // P of step n goes to the single P region: the P.V of step n-1 must be done with it
+    const uint32_t tP = tmem + lane_base + C::kColP;
+    auto wait_p_free = [&](int64_t n) -> bool {
+      if (n < 1) return true;
+      const int64_t m = n - 1;
+      if (!mbar_wait_bounded(&o_done[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) return false;
+      tc_fence_after();
       return true;
     };
     // hand P (and U) of step n to the MMA warp
     auto release_step = [&](int64_t n) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) PASA_TRACE_MARK(12 + (warp - 2), n);
+      if (lane == 0 && warp < 11) PASA_TRACE_MARK(12 + (warp - 3), n);
       if (lane == 0) mbar_arrive(&p_ready[n & 1]);
     };
 
@@ -488,34 +515,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       if (!wait_scores(n, tS)) { ok = false; break; }
       {
         // ---------------- Phase 1: a pair of exact blocks ----------------
-        // this thread owns columns [32 ch, 32 ch + 32) of each block
         const uint32_t e0 = ulist[2 * n];
         const uint32_t e1 = (2 * n + 1 < nU) ? uint32_t(ulist[2 * n + 1]) : 0u;  // lone last block: no bits
-        const bool act0 = live && ((e0 >> half) & 1u);  // uniform per warp
+        const bool act0 = live && ((e0 >> half) & 1u);  // uniform per warp (and per quadrant)
         const bool act1 = live && ((e1 >> half) & 1u);
-        uint32_t pk0[16], pk1[16];
+        uint32_t pk0[kPC / 2], pk1[kPC / 2];
+        uint32_t s0[kPC], s1[kPC];
+        if (act0) tmem_ld<kPC>(tS + part * kPC, s0);
+        if (act1) tmem_ld<kPC>(tS + 64 + part * kPC, s1);
+        tmem_wait_ld();
+        // the scores are in registers: the S buffer may take the scores of step n + 2
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[n & 1]);
         if (act0 || act1) {
-          uint32_t s0[32], s1[32];
-          if (act0) tmem_ld32(tS + ch * 32, s0);
-          if (act1) tmem_ld32(tS + 64 + ch * 32, s1);
-          tmem_wait_ld();
-#ifdef PASA_TRACE
-          if (warp == 2) {  // trace only: force the loaded registers to be consumed before stamping
-            uint32_t x = (act0 ? s0[0] ^ s0[31] : 0u) ^ (act1 ? s1[0] ^ s1[31] : 0u);
-            asm volatile("" : "+r"(x));
-            if (x == 0x7fffffffu && lane == 33) PASA_TRACE_MARK(27, n);
-          }
-#endif
-          if (warp == 2 && lane == 0) PASA_TRACE_MARK(24, n);
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(24, n);
           // key rows >= T are masked (:178); only the last block has them
-          if (act0 && int64_t(e0 >> 2) == NT - 1) mask_tail32(s0, int(last_len) - ch * 32);
-          if (act1 && int64_t(e1 >> 2) == NT - 1) mask_tail32(s1, int(last_len) - ch * 32);
+          if (act0 && int64_t(e0 >> 2) == NT - 1) mask_tail<kPC>(s0, int(last_len) - part * kPC);
+          if (act1 && int64_t(e1 >> 2) == NT - 1) mask_tail<kPC>(s1, int(last_len) - part * kPC);
           float mx = -INFINITY;
-          if (act0) mx = max_tree32(s0);
-          if (act1) mx = fmaxf(mx, max_tree32(s1));
-          if (warp == 2 && lane == 0) PASA_TRACE_MARK(25, n);
-          mx = fmaxf(mx, exchange(mx)) * sm_scale;  // max commutes with the positive scale
-          if (warp == 2 && lane == 0) PASA_TRACE_MARK(26, n);
+          if (act0) mx = max_tree<kPC>(s0);
+          if (act1) mx = fmaxf(mx, max_tree<kPC>(s1));
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(25, n);
+          mx = row_reduce(mx, true) * sm_scale;  // max commutes with the positive scale
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(26, n);
           m_true = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;
           const bool need = grow && (m_used != -INFINITY);
@@ -526,32 +549,33 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           l1 *= alpha;
           if (grow) m_used = mx;
           if (act0) {
-            l1 += exp2_pack32(s0, sm_scale, -m_used, pk0);
+            l1 += exp2_pack<kPC>(s0, sm_scale, -m_used, pk0);
           } else {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) pk0[c] = 0u;
+            for (int c = 0; c < kPC / 2; ++c) pk0[c] = 0u;
           }
           if (act1) {
-            l1 += exp2_pack32(s1, sm_scale, -m_used, pk1);
+            l1 += exp2_pack<kPC>(s1, sm_scale, -m_used, pk1);
           } else {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) pk1[c] = 0u;
+            for (int c = 0; c < kPC / 2; ++c) pk1[c] = 0u;
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) { pk0[c] = 0u; pk1[c] = 0u; }
+          for (int c = 0; c < kPC / 2; ++c) { pk0[c] = 0u; pk1[c] = 0u; }
         }
-        if (warp == 2 && lane == 0) PASA_TRACE_MARK(27, n);
-        tmem_st16(tS + ch * 16, pk0);       // keys [32 ch, 32 ch + 32) of block 0
-        tmem_st16(tS + 32 + ch * 16, pk1);  // keys [64 + 32 ch, ...) of block 1
+        if (warp == 3 && lane == 0) PASA_TRACE_MARK(27, n);
+        if (!wait_p_free(n)) ok = false;
+        tmem_st<kPC / 2>(tP + part * (kPC / 2), pk0);       // keys [kPC part, kPC part + kPC) of block 0
+        tmem_st<kPC / 2>(tP + 32 + part * (kPC / 2), pk1);  // the same keys of block 1
         tmem_wait_st();
       }
       release_step(n);
     }
 
-    uint32_t qpk[DH / 2];  // this row's half of Q (packed bf16), read back from TMEM for phase 2
+    uint32_t qpk[DQ / 2];  // this row's part of Q (packed bf16), read back from TMEM for phase 2
     if (ok) {
-      tmem_ld<DH / 2>(tmem + lane_base + C::kColQ + ch * (DH / 2), qpk);
+      tmem_ld<DQ / 2>(tmem + lane_base + C::kColQ + part * (DQ / 2), qpk);
       tmem_wait_ld();
     }
     for (int64_t n = nP; n < total && ok; ++n) {
@@ -560,21 +584,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       {
         // ---------------- Phase 2: group g ----------------
         const int64_t g = n - nP;
-        uint32_t pk[8];
-        uint32_t upk[DH / 2];
+        uint32_t pk[kGC / 2];
+        uint32_t upk[DQ / 2];
         if (live) {
-          uint32_t sv[16];
-          tmem_ld16(tS + ch * 16, sv);
+          uint32_t sv[kGC];
+          tmem_ld<kGC>(tS + part * kGC, sv);
           tmem_wait_ld();
-          const uint32_t word = maskw[half * kMaxNG + g] >> (ch * 16);
-          const int64_t jb0 = g * kGroup + ch * 16;
+          const uint32_t word = maskw[half * kMaxNG + g] >> (part * kGC);
+          const int64_t jb0 = g * kGroup + part * kGC;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
+          for (int c = 0; c < kGC; ++c) {
             const bool valid = (jb0 + c < NT) && !((word >> c) & 1u);  // :228
             if (!valid) sv[c] = __float_as_uint(-INFINITY);
           }
-          float mx = max_tree16(sv);
-          mx = fmaxf(mx, exchange(mx));
+          float mx = max_tree<kGC>(sv);
+          mx = row_reduce(mx, true);
           mx = (mx == -INFINITY) ? mx : mx * sm_scale;
           const float m_true_new = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;  // m_used is finite for live rows here
@@ -584,16 +608,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           }
           l1 *= alpha;
           if (grow) m_used = mx;
-          float p[16];
+          float p[kGC];
           const float negm = -m_used;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) p[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
+          for (int c = 0; c < kGC; ++c) p[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
           float psum = 0.f, wsum;
           {
             float a0 = 0.f, a1 = 0.f, extra = 0.f;
             const int64_t last_rel = NT - 1 - jb0;  // column of the ragged last block, if in range
 #pragma unroll
-            for (int c = 0; c < 16; c += 2) {
+            for (int c = 0; c < kGC; c += 2) {
               a0 += p[c]; a1 += p[c + 1];
               extra += (c == last_rel) ? p[c] : ((c + 1 == last_rel) ? p[c + 1] : 0.f);
             }
@@ -602,25 +626,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             wsum = psum * float(kBlock) + extra * float(last_len - kBlock);
           }
 #pragma unroll
-          for (int c = 0; c < 16; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
-          psum += exchange(psum);
+          for (int c = 0; c < kGC; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
+          psum = row_reduce(psum, false);
           // the reference's probabilities use the exact running max (:237, :243)
           gl += wsum * fast_exp2(m_used - m_true_new);
           m_true = m_true_new;
           const float w = psum * scale32;  // :253
 #pragma unroll
-          for (int x = 0; x < DH / 2; ++x) {
+          for (int x = 0; x < DQ / 2; ++x) {
             const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qpk[x]));
             upk[x] = pack_bf16x2(qf.x * w, qf.y * w);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) pk[c] = 0u;
+          for (int c = 0; c < kGC / 2; ++c) pk[c] = 0u;
 #pragma unroll
-          for (int x = 0; x < DH / 2; ++x) upk[x] = 0u;
+          for (int x = 0; x < DQ / 2; ++x) upk[x] = 0u;
         }
-        tmem_st8(tS + ch * 8, pk);
-        tmem_st<DH / 2>(tS + C::kColU + ch * (DH / 2), upk);
+        if (!wait_p_free(n)) ok = false;
+        tmem_st<kGC / 2>(tP + part * (kGC / 2), pk);
+        tmem_st<DQ / 2>(tS + C::kColU + part * (DQ / 2), upk);
         tmem_wait_st();
       }
       release_step(n);
@@ -636,18 +661,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     const int64_t t = blk * kBlock + (r & 63);
     const bool wok = __all_sync(0xffffffffu, ok);
     if (live) {
-      // partners combine their partial sums (both take part even after a failure)
-      const float l_tot = l1 + exchange(l1);
-      const float g_tot = gl + exchange(gl);
+      // the row's threads combine their partial sums (all take part even after a failure)
+      const float l_tot = row_reduce(l1, false);
+      const float g_tot = row_reduce(gl, false);
       if (wok) {  // warp-uniform: tcgen05.ld is warp-collective
         const bool store = t < P.T;
         const float denom = l_tot + g_tot * fast_exp2(m_true - m_used);
         const float inv = 1.0f / denom;
-        __nv_bfloat16* orow = P.o + (bh * P.T + t) * D + ch * DH;
+        __nv_bfloat16* orow = P.o + (bh * P.T + t) * D + part * DQ;
 #pragma unroll
-        for (int c0 = 0; c0 < DH; c0 += 16) {
+        for (int c0 = 0; c0 < DQ; c0 += 16) {
           uint32_t v[16];
-          tmem_ld16(tmem + lane_base + C::kColO + ch * DH + c0, v);
+          tmem_ld16(tmem + lane_base + C::kColO + part * DQ + c0, v);
           tmem_wait_ld();
           uint4 out[2];
           uint32_t* ow = reinterpret_cast<uint32_t*>(out);

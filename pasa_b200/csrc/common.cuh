@@ -258,21 +258,38 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// Whole-array TMEM load / store of N = 16 or 32 consecutive columns.
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
-  if constexpr (N == 32) tmem_ld32(taddr, r); else tmem_ld16(taddr, r);
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
-template <int N>
-__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) {
-  if constexpr (N == 32) tmem_st32(taddr, r); else tmem_st16(taddr, r);
-}
-
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
       :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
+}
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};"
+               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]) : "memory");
+}
+
+// Whole-array TMEM load / store of N consecutive columns (load: 8, 16, 32;
+// store: 4, 8, 16, 32).
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 8 || N == 16 || N == 32, "tmem_ld width");
+  if constexpr (N == 32) tmem_ld32(taddr, r);
+  else if constexpr (N == 16) tmem_ld16(taddr, r);
+  else tmem_ld8(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) {
+  static_assert(N == 4 || N == 8 || N == 16 || N == 32, "tmem_st width");
+  if constexpr (N == 32) tmem_st32(taddr, r);
+  else if constexpr (N == 16) tmem_st16(taddr, r);
+  else if constexpr (N == 8) tmem_st8(taddr, r);
+  else tmem_st4(taddr, r);
 }
 
 // Named barrier over `nthreads` threads (multiple of 32); id 0 is __syncthreads.
@@ -298,6 +315,11 @@ __device__ __forceinline__ float max_tree32(const uint32_t (&v)[32]) {
   const float c = fmax3(m[6], m[7], m[8]), d = fmax3(m[9], m[10], m[11]);
   return fmaxf(fmax3(a, b, c), d);
 }
+__device__ __forceinline__ float max_tree8(const uint32_t (&v)[8]) {
+  const float a = fmax3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+  const float b = fmax3(__uint_as_float(v[3]), __uint_as_float(v[4]), __uint_as_float(v[5]));
+  return fmax3(a, b, fmaxf(__uint_as_float(v[6]), __uint_as_float(v[7])));
+}
 __device__ __forceinline__ float max_tree16(const uint32_t (&v)[16]) {
   float m[6];
 #pragma unroll
@@ -309,15 +331,25 @@ __device__ __forceinline__ float max_tree16(const uint32_t (&v)[16]) {
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi);
 
-// p_c = 2^(s_c * scale + negm) for 32 raw fp32 scores; packs bf16 pairs into
-// pk and returns the fp32 sum of the p_c.  The scale/shift and the sums use
-// the sm_100 packed fp32 pair instructions.
-__device__ __forceinline__ float exp2_pack32(const uint32_t (&sv)[32], float scale, float negm,
-                                             uint32_t (&pk)[16]) {
+template <int N>
+__device__ __forceinline__ float max_tree(const uint32_t (&v)[N]) {
+  static_assert(N == 8 || N == 16 || N == 32, "max_tree width");
+  if constexpr (N == 32) return max_tree32(v);
+  else if constexpr (N == 16) return max_tree16(v);
+  else return max_tree8(v);
+}
+
+// p_c = 2^(s_c * scale + negm) for N (a multiple of 4) raw fp32 scores;
+// packs bf16 pairs into pk and returns the fp32 sum of the p_c.  The
+// scale/shift and the sums use the sm_100 packed fp32 pair instructions.
+template <int N>
+__device__ __forceinline__ float exp2_pack(const uint32_t (&sv)[N], float scale, float negm,
+                                           uint32_t (&pk)[N / 2]) {
+  static_assert(N % 4 == 0, "exp2_pack width");
   const float2 sc = make_float2(scale, scale), nm = make_float2(negm, negm);
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int c = 0; c < 32; c += 4) {
+  for (int c = 0; c < N; c += 4) {
     float2 x01 = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc, nm);
     float2 x23 = __ffma2_rn(make_float2(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3])), sc, nm);
     x01.x = fast_exp2(x01.x); x01.y = fast_exp2(x01.y);
