@@ -33,8 +33,10 @@
 //     The softmax frees an S buffer as soon as its scores are in registers,
 //     so the score MMAs of step n+2 overlap the softmax and P.V of step n.
 //     In phase 2 the first-order operand U = bf16(w_t q_t) (w_t = scale *
-//     sum of the group's probabilities) sits in the S buffer's upper half and
-//     U.H_g is accumulated straight into O.
+//     sum of the group's probabilities) sits in the upper half of the other
+//     S buffer (group scores are only 32 columns wide) and U.H_g is
+//     accumulated straight into O; P_g alternates between two 16-column
+//     slots, so a group's softmax never waits for the previous group's P.V.
 //   * softmax rescales O only when a row max grows by more than 2^8
 //     (exact either way: O and l share the stale max); the exact running max
 //     is tracked separately to reproduce g_l.
@@ -81,7 +83,7 @@ struct Cfg {
   static constexpr uint32_t kColQ = 128;
   static constexpr uint32_t kColP = 192;                // P (packed bf16) of the step in flight
   static constexpr uint32_t kColS0 = 256;               // S buffer b at kColS0 + 128 b
-  static constexpr uint32_t kColU = 64;                 // phase 2: U inside the S buffer
+  static constexpr uint32_t kColU = 64;                 // phase 2: U of step n in S buffer (n + 1) & 1
   static constexpr uint32_t kTmemCols = 512;
   // shared memory carve-up (offsets from a 1024-aligned base).  Q is staged
   // inside ring slot 2 and copied to TMEM before that slot is first filled.
@@ -159,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* s_full = q_tmem + 1;   // [2]
   uint64_t* p_ready = s_full + 2;  // [2]
   uint64_t* o_done = p_ready + 2;  // [2]
-  uint64_t* s_free = o_done + 2;   // [2] phase-1 scores of the buffer are in registers
+  uint64_t* s_free = o_done + 2;   // [2] the buffer's scores are in registers
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffSlot);
   __shared__ uint32_t s_nu;
 
@@ -329,9 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     // the tensor core retires an M128 N128 K16 step, so the score MMAs
     // (warp 1) and the P.V / correction MMAs (warp 2) have an issuer each.
     // Their only shared resource is the S buffer: S(n) may overwrite buffer
-    // n & 1 once the softmax has pulled the phase-1 scores of step n-2 into
-    // registers (s_free), or, for a phase-2 step n-2, once its P.V, which
-    // reads U from that buffer, has completed (o_done).
+    // n & 1 once the softmax has pulled the scores of step n-2 into registers
+    // (s_free).  Phase-2 score MMAs are N = 32 and leave the buffer's upper
+    // half to U of step n-1.
     if (lane == 0) {
       constexpr uint32_t idS128 = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idS32 = umma_idesc_bf16(128, 32, false, false);
@@ -348,9 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         for (int64_t n = 0; n < total && ok; ++n) {
           if (n >= 2) {
             const int64_t m = n - 2;
-            const bool freed = (m < nP) ? mbar_wait_bounded(&s_free[m & 1], uint32_t((m >> 1) & 1), kPollLimit)
-                                        : mbar_wait_bounded(&o_done[m & 1], uint32_t((m >> 1) & 1), kPollLimit);
-            if (!freed) { ok = false; break; }
+            if (!mbar_wait_bounded(&s_free[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) { ok = false; break; }
           }
           const bool landed = (n < nP)
               ? mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)
@@ -384,7 +384,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           PASA_TRACE_MARK(2, m);
           tc_fence_after();
           const uint32_t st = slot_addr(m);
-          const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(m & 1);
           if (m < nP) {  // O += P . [V_j0; V_j1], K = 128
 #pragma unroll
             for (int kk = 0; kk < 2 * kBlock / 16; ++kk) {
@@ -393,15 +392,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             }
             tc_commit(&empty1[m % C::kS1]);
           } else {       // O += P_g . vc_g + U_g . H_g
+            const uint32_t tPg = tmem + C::kColP + 16u * uint32_t(m & 1);
+            const uint32_t tU = tmem + C::kColS0 + 128u * uint32_t((m + 1) & 1) + C::kColU;
 #pragma unroll
             for (int kk = 0; kk < kGroup / 16; ++kk) {
               const uint64_t bd = umma_desc_sw128(st + C::kCBytes + kk * 2048, C::kCBytes / C::kBoxes, 1024);
-              mma_ts(tmem + C::kColO, tmem + C::kColP + kk * 8, bd, idPV, 1u);
+              mma_ts(tmem + C::kColO, tPg + kk * 8, bd, idPV, 1u);
             }
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint64_t bd = umma_desc_sw128(st + 2 * C::kCBytes + kk * 2048, C::kHBytes / C::kBoxes, 1024);
-              mma_ts(tmem + C::kColO, tS + C::kColU + kk * 8, bd, idPV, 1u);
+              mma_ts(tmem + C::kColO, tU + kk * 8, bd, idPV, 1u);
             }
             tc_commit(&empty2[(m - nP) % C::kS2]);
           }
@@ -493,11 +494,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(b);
       return true;
     };
-    // P of step n goes to the single P region: the P.V of step n-1 must be done with it
+    // P of a phase-1 step fills the P region, so the P.V of step n-1 must be
+    // done with it.  A phase-2 step n writes P_g to half n & 1 of the region's
+    // first 32 columns and U to S buffer (n + 1) & 1, both last read by the
+    // P.V of step n-2 (of step n-1 for the first group, after the full-width P).
     const uint32_t tP = tmem + lane_base + C::kColP;
     auto wait_p_free = [&](int64_t n) -> bool {
-      if (n < 1) return true;
-      const int64_t m = n - 1;
+      const int64_t lag = (n <= nP) ? 1 : 2;
+      if (n < lag) return true;
+      const int64_t m = n - lag;
       if (!mbar_wait_bounded(&o_done[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) return false;
       tc_fence_after();
       return true;
@@ -531,8 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         if (act0 || act1) {
           if (warp == 3 && lane == 0) PASA_TRACE_MARK(24, n);
           // key rows >= T are masked (:178); only the last block has them
-          if (act0 && int64_t(e0 >> 2) == NT - 1) mask_tail<kPC>(s0, int(last_len) - part * kPC);
-          if (act1 && int64_t(e1 >> 2) == NT - 1) mask_tail<kPC>(s1, int(last_len) - part * kPC);
+          if (act0 && int(e0 >> 2) == int(NT) - 1) mask_tail<kPC>(s0, int(last_len) - part * kPC);
+          if (act1 && int(e1 >> 2) == int(NT) - 1) mask_tail<kPC>(s1, int(last_len) - part * kPC);
           float mx = -INFINITY;
           if (act0) mx = max_tree<kPC>(s0);
           if (act1) mx = fmaxf(mx, max_tree<kPC>(s1));
@@ -586,19 +591,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         const int64_t g = n - nP;
         uint32_t pk[kGC / 2];
         uint32_t upk[DQ / 2];
+        uint32_t sv[kGC];
+        if (live) tmem_ld<kGC>(tS + part * kGC, sv);
+        tmem_wait_ld();
+        // the scores are in registers: the S buffer may take the scores of step n + 2
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[n & 1]);
+        if (warp == 3 && lane == 0) PASA_TRACE_MARK(24, n);
         if (live) {
-          uint32_t sv[kGC];
-          tmem_ld<kGC>(tS + part * kGC, sv);
-          tmem_wait_ld();
+          // columns of selected blocks or of blocks >= NT are masked (:228)
+          const int jb0 = int(g) * kGroup + part * kGC;  // NT <= kMaxNT fits in int
+          const int lim = int(NT) - jb0;
           const uint32_t word = maskw[half * kMaxNG + g] >> (part * kGC);
-          const int64_t jb0 = g * kGroup + part * kGC;
 #pragma unroll
-          for (int c = 0; c < kGC; ++c) {
-            const bool valid = (jb0 + c < NT) && !((word >> c) & 1u);  // :228
-            if (!valid) sv[c] = __float_as_uint(-INFINITY);
-          }
+          for (int c = 0; c < kGC; ++c)
+            if (c >= lim || ((word >> c) & 1u)) sv[c] = __float_as_uint(-INFINITY);
           float mx = max_tree<kGC>(sv);
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(23, n);
           mx = row_reduce(mx, true);
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(25, n);
           mx = (mx == -INFINITY) ? mx : mx * sm_scale;
           const float m_true_new = fmaxf(m_true, mx);
           const bool grow = mx > m_used + kRescaleThresh;  // m_used is finite for live rows here
@@ -612,14 +624,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           const float negm = -m_used;
 #pragma unroll
           for (int c = 0; c < kGC; ++c) p[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(26, n);
           float psum = 0.f, wsum;
           {
             float a0 = 0.f, a1 = 0.f, extra = 0.f;
-            const int64_t last_rel = NT - 1 - jb0;  // column of the ragged last block, if in range
+            // bit of the ragged last block's column, if it is one of this thread's
+            // (a bit test, not an index: p[] must stay in registers)
+            const uint32_t lastbit = (lim >= 1 && lim <= kGC) ? (1u << (lim - 1)) : 0u;
 #pragma unroll
             for (int c = 0; c < kGC; c += 2) {
               a0 += p[c]; a1 += p[c + 1];
-              extra += (c == last_rel) ? p[c] : ((c + 1 == last_rel) ? p[c + 1] : 0.f);
+              extra += ((lastbit >> c) & 1u) ? p[c] : (((lastbit >> (c + 1)) & 1u) ? p[c + 1] : 0.f);
             }
             psum = a0 + a1;
             // the ragged last block has its own length (:220)
@@ -628,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
           for (int c = 0; c < kGC; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
           psum = row_reduce(psum, false);
+          if (warp == 3 && lane == 0) PASA_TRACE_MARK(27, n);
           // the reference's probabilities use the exact running max (:237, :243)
           gl += wsum * fast_exp2(m_used - m_true_new);
           m_true = m_true_new;
@@ -643,10 +659,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
           for (int x = 0; x < DQ / 2; ++x) upk[x] = 0u;
         }
+        if (warp == 3 && lane == 0) PASA_TRACE_MARK(20, n);
         if (!wait_p_free(n)) ok = false;
-        tmem_st<kGC / 2>(tP + part * (kGC / 2), pk);
-        tmem_st<DQ / 2>(tS + C::kColU + part * (DQ / 2), upk);
+        if (warp == 3 && lane == 0) PASA_TRACE_MARK(21, n);
+        tmem_st<kGC / 2>(tP + 16u * uint32_t(n & 1) + part * (kGC / 2), pk);
+        tmem_st<DQ / 2>(tmem + lane_base + C::kColS0 + 128u * uint32_t((n + 1) & 1) + C::kColU + part * (DQ / 2),
+                        upk);
         tmem_wait_st();
+        if (warp == 3 && lane == 0) PASA_TRACE_MARK(22, n);
       }
       release_step(n);
     }

@@ -109,6 +109,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with an explicit suspend-time hint (ns): the thread sleeps in
+// hardware until the phase completes or the hint elapses, instead of
+// re-issuing the probe and taking issue slots from its sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+  return ok != 0;
+}
+
 // Non-blocking probe of a phase (mbarrier.test_wait).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -134,6 +147,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = sm_cycles();
   for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (sm_cycles() - t0 > limit) return false;
+  }
+}
+
+// Bounded wait with a sleep between probes, for helper threads (TMA
+// producer, MMA issuers) that wait long and often: a probe loop would take
+// issue slots from the softmax warps sharing the thread's sub-partition.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
+                                                  uint64_t limit = kWaitLimitCycles) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = sm_cycles();
+  for (;;) {
+    __nanosleep(sleep_ns);
     if (mbar_try_wait(bar, parity)) return true;
     if (sm_cycles() - t0 > limit) return false;
   }
