@@ -623,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           float p[kGC];
           const float negm = -m_used;
 #pragma unroll
-          for (int c = 0; c < kGC; ++c) p[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
+          for (int c = 0; c < kGC; ++c) p[c] = exp2_ftz(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
           if (warp == 3 && lane == 0) PASA_TRACE_MARK(26, n);
           float psum = 0.f, wsum;
           {

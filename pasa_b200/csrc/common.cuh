@@ -40,6 +40,17 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// The same approximation with subnormal inputs and results flushed to zero
+// (ex2.approx.ftz.f32, one MUFU instruction; the non-flushing form needs
+// extra instructions around it).  For the softmax probabilities a result
+// below 2^-126 is irrelevant: it rounds into a bf16 P that contributes
+// nothing next to the row maximum's 2^0.
+__device__ __forceinline__ float exp2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---------------------------------------------------------------------------
 // workspace layout used by pasa_forward (all offsets 256-byte aligned)
 // ---------------------------------------------------------------------------
@@ -379,8 +390,8 @@ __device__ __forceinline__ float exp2_pack(const uint32_t (&sv)[N], float scale,
   for (int c = 0; c < N; c += 4) {
     float2 x01 = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc, nm);
     float2 x23 = __ffma2_rn(make_float2(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3])), sc, nm);
-    x01.x = fast_exp2(x01.x); x01.y = fast_exp2(x01.y);
-    x23.x = fast_exp2(x23.x); x23.y = fast_exp2(x23.y);
+    x01.x = exp2_ftz(x01.x); x01.y = exp2_ftz(x01.y);
+    x23.x = exp2_ftz(x23.x); x23.y = exp2_ftz(x23.y);
     pk[c / 2] = pack_bf16x2(x01.x, x01.y);
     pk[c / 2 + 1] = pack_bf16x2(x23.x, x23.y);
     acc0 = __fadd2_rn(acc0, x01);
