@@ -92,8 +92,9 @@ struct Cfg {
   static constexpr int kOffUnion = kOffRing + kRingBytes;            // u16 [kMaxNT]
   static constexpr int kOffMask = kOffUnion + kMaxNT * 2;            // u32 [2][kMaxNG]
   static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][kParts][128]
-  static constexpr int kOffBar = kOffXch + 2 * kParts * kRowsPerTile * 4;
-  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 2 + 2 + 2 + 2 + 2;
+  static constexpr int kOffHand = kOffXch + 2 * kParts * kRowsPerTile * 4;  // f32 [2 parts][m_used, m_true][128]
+  static constexpr int kOffBar = kOffHand + 2 * 2 * kRowsPerTile * 4;
+  static constexpr int kNumBars = 2 * kS1 + 2 * kS2 + 2 + 2 + 2 + 2 + 2 + 2 + 2;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
   static_assert(kOffQ + kQBytes <= kRingBytes, "Q staging must fit in the ring");
@@ -122,13 +123,17 @@ struct Params {
 #ifdef PASA_TRACE
 constexpr int kTraceSteps = 1024;
 __device__ unsigned long long g_pasa_trace[30][kTraceSteps];
+__device__ unsigned int g_pasa_trace_cta[2];  // (blockIdx.x, blockIdx.y) of the traced CTA
+__device__ unsigned long long g_pasa_trace_ctl[8];  // entry, set-up done, softmax done, exit (per traced CTA)
+#define PASA_TRACE_CTL(i) do { if (pasa_traced) g_pasa_trace_ctl[(i)] = clock64(); } while (0)
+// pasa_traced: a bool computed once per CTA at kernel entry
 #define PASA_TRACE_MARK(ev, step)                                                        \
   do {                                                                                    \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (step) < kTraceSteps)                       \
-      g_pasa_trace[(ev)][(step)] = clock64();                                             \
+    if (pasa_traced && (step) < kTraceSteps) g_pasa_trace[(ev)][(step)] = clock64();      \
   } while (0)
 #else
 #define PASA_TRACE_MARK(ev, step) do { } while (0)
+#define PASA_TRACE_CTL(i) do { } while (0)
 #endif
 
 __device__ __forceinline__ void report(uint32_t* err) {
@@ -151,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint16_t* ulist = reinterpret_cast<uint16_t*>(sm + C::kOffUnion);  // (block << 2) | half bits
   uint32_t* maskw = reinterpret_cast<uint32_t*>(sm + C::kOffMask);  // [2][kMaxNG]
   float* xch = reinterpret_cast<float*>(sm + C::kOffXch);
+  float* hand = reinterpret_cast<float*>(sm + C::kOffHand);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
   uint64_t* full1 = bars;
   uint64_t* empty1 = full1 + C::kS1;
@@ -161,11 +167,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* s_full = q_tmem + 1;   // [2]
   uint64_t* p_ready = s_full + 2;  // [2]
   uint64_t* o_done = p_ready + 2;  // [2]
-  uint64_t* s_free = o_done + 2;   // [2] the buffer's scores are in registers
+  uint64_t* s_free = o_done + 2;   // [2] the buffer's scores are in registers (phase 1)
+  uint64_t* s2_free = s_free + 2;  // [2 parts] phase 2: the part's group scores are in registers
+  uint64_t* p2_ready = s2_free + 2;  // [2 parts] phase 2: the part's P_g and U are in TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffSlot);
   __shared__ uint32_t s_nu;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#ifdef PASA_TRACE
+  const bool pasa_traced = blockIdx.x == g_pasa_trace_cta[0] && blockIdx.y == g_pasa_trace_cta[1];
+  if (tid == 0) PASA_TRACE_CTL(0);
+#endif
   const int64_t pair = blockIdx.x, bh = blockIdx.y;
   const int64_t NT = P.NT, NG = P.NG;
   const int64_t blkA = 2 * pair, blkB = 2 * pair + 1;
@@ -180,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1); mbar_init(&p_ready[b], kSoftmaxWarps); mbar_init(&o_done[b], 1);
       mbar_init(&s_free[b], kSoftmaxWarps);
+      mbar_init(&s2_free[b], kSoftmaxWarps / 2); mbar_init(&p2_ready[b], kSoftmaxWarps / 2);
     }
     fence_barrier_init();
   }
@@ -256,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) PASA_TRACE_CTL(1);
   const int64_t nU = s_nu;
   const int64_t nP = (nU + 1) / 2;  // phase-1 steps: two union blocks each (a lone last block pairs with itself)
   const int64_t total = nP + NG;
@@ -263,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   if (warp == 0) {
     // ================= TMA producer =================
 #ifdef PASA_TRACE
-    if (lane == 1 && blockIdx.x == 0 && blockIdx.y == 0) {  // trace only: stamp data arrival (event 3)
+    if (lane == 1 && pasa_traced) {  // trace only: stamp data arrival (event 3)
       for (int64_t n = 0; n < nP && n < kTraceSteps; ++n)
         if (mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)) PASA_TRACE_MARK(3, n);
     }
@@ -350,7 +364,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         for (int64_t n = 0; n < total && ok; ++n) {
           if (n >= 2) {
             const int64_t m = n - 2;
-            if (!mbar_wait_bounded(&s_free[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) { ok = false; break; }
+            const int64_t g2 = m - nP;  // phase-2 group of step m, if any
+            const bool freed = (m < nP) ? mbar_wait_bounded(&s_free[m & 1], uint32_t((m >> 1) & 1), kPollLimit)
+                                        : mbar_wait_bounded(&s2_free[g2 & 1], uint32_t((g2 >> 1) & 1), kPollLimit);
+            if (!freed) { ok = false; break; }
           }
           const bool landed = (n < nP)
               ? mbar_wait_bounded(&full1[n % C::kS1], uint32_t((n / C::kS1) & 1), kPollLimit)
@@ -380,7 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         }
       } else {
         for (int64_t m = 0; m < total && ok; ++m) {
-          if (!mbar_wait_bounded(&p_ready[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) { ok = false; break; }
+          const int64_t g2 = m - nP;  // phase-2 group of step m, if any
+          const bool ready = (m < nP) ? mbar_wait_bounded(&p_ready[m & 1], uint32_t((m >> 1) & 1), kPollLimit)
+                                      : mbar_wait_bounded(&p2_ready[g2 & 1], uint32_t((g2 >> 1) & 1), kPollLimit);
+          if (!ready) { ok = false; break; }
           PASA_TRACE_MARK(2, m);
           tc_fence_after();
           const uint32_t st = slot_addr(m);
@@ -416,9 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   } else {
     // ================= softmax / correction (warps 3 .. 3 + kSoftmaxWarps) =================
     // kParts threads per query row (TMEM lane): thread `part` owns columns
-    // [kPC part, kPC part + kPC) of both key blocks of a phase-1 step,
-    // columns [kGC part, kGC part + kGC) of a phase-2 group, and output
-    // columns [DQ part, DQ part + DQ).  The kParts warps of a lane quadrant combine
+    // [kPC part, kPC part + kPC) of both key blocks of a phase-1 step and
+    // output columns [DQ part, DQ part + DQ); in phase 2 it owns every other
+    // group of its row.  The kParts warps of a lane quadrant combine
     // row maxima and sums through shared memory.
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
     const int part = (warp - 3) >> 2;          // column part of this warp
@@ -432,7 +452,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     const int64_t last_len = P.T - (NT - 1) * kBlock;
     constexpr int DQ = D / kParts;             // Q / output columns per thread
     constexpr int kPC = kBlock / kParts;       // score columns per key block per thread
-    constexpr int kGC = kGroup / kParts;       // group columns per thread
     float m_true = -INFINITY, m_used = -INFINITY, l1 = 0.f, gl = 0.f;
     uint32_t xslot = 0;
     // combine one value per thread across the row's kParts threads (fixed order)
@@ -485,6 +504,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       return true;
     };
 
+    // phase 2: one thread owns the row, so it rescales all D columns of O
+    auto rescale_o_all = [&](int64_t n, float alpha) -> bool {
+      if (n >= 1) {
+        const int64_t m = n - 1;
+        if (!mbar_wait_bounded(&o_done[m & 1], uint32_t((m >> 1) & 1), kPollLimit)) return false;
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_base + C::kColO + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int x = 0; x < 16; ++x) v[x] = __float_as_uint(__uint_as_float(v[x]) * alpha);
+        tmem_st16(tmem + lane_base + C::kColO + c0, v);
+      }
+      tmem_wait_st();
+      return true;
+    };
+
     // wait for the scores of step n; returns this thread's S-buffer address
     auto wait_scores = [&](int64_t n, uint32_t& tS) -> bool {
       const int b = int(n & 1);
@@ -494,6 +533,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(b);
       return true;
     };
+    // After a failed wait (ok false) the loops keep going without waiting, so
+    // every warp still takes part in every named barrier and none is stranded.
     // P of a phase-1 step fills the P region, so the P.V of step n-1 must be
     // done with it.  A phase-2 step n writes P_g to half n & 1 of the region's
     // first 32 columns and U to S buffer (n + 1) & 1, both last read by the
@@ -515,9 +556,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       if (lane == 0) mbar_arrive(&p_ready[n & 1]);
     };
 
-    for (int64_t n = 0; n < nP && ok; ++n) {
-      uint32_t tS;
-      if (!wait_scores(n, tS)) { ok = false; break; }
+    for (int64_t n = 0; n < nP; ++n) {
+      uint32_t tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(n & 1);
+      if (ok && !wait_scores(n, tS)) ok = false;
       {
         // ---------------- Phase 1: a pair of exact blocks ----------------
         const uint32_t e0 = ulist[2 * n];
@@ -549,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           const bool need = grow && (m_used != -INFINITY);
           const float alpha = need ? fast_exp2(m_used - mx) : 1.0f;
           if (__any_sync(0xffffffffu, need)) {  // tcgen05.ld/st are warp-collective
-            if (!rescale_o(n, alpha)) ok = false;
+            if (ok && !rescale_o(n, alpha)) ok = false;
           }
           l1 *= alpha;
           if (grow) m_used = mx;
@@ -570,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           for (int c = 0; c < kPC / 2; ++c) { pk0[c] = 0u; pk1[c] = 0u; }
         }
         if (warp == 3 && lane == 0) PASA_TRACE_MARK(27, n);
-        if (!wait_p_free(n)) ok = false;
+        if (ok && !wait_p_free(n)) ok = false;
         tmem_st<kPC / 2>(tP + part * (kPC / 2), pk0);       // keys [kPC part, kPC part + kPC) of block 0
         tmem_st<kPC / 2>(tP + 32 + part * (kPC / 2), pk1);  // the same keys of block 1
         tmem_wait_st();
@@ -578,97 +619,118 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       release_step(n);
     }
 
-    uint32_t qpk[DQ / 2];  // this row's part of Q (packed bf16), read back from TMEM for phase 2
-    if (ok) {
-      tmem_ld<DQ / 2>(tmem + lane_base + C::kColQ + part * (DQ / 2), qpk);
+    // ---------------- Phase 2: groups, ping-pong between the two column parts ----------------
+    // The warps of part p take the groups g with g % 2 == p, one thread per row
+    // owning all kGroup columns of its group, so consecutive groups overlap.
+    // The reference's running maxima are sequential over groups (:237-243):
+    // each group hands (m_used, m_true) of its rows to the next group's warps
+    // through shared memory and a named barrier per lane quadrant and
+    // direction (arrive by the producer, sync by the consumer).
+    static_assert(kParts == 2, "phase-2 ping-pong pairs the two column parts");
+    float m_applied = m_used;  // the maximum this thread's l1 is scaled to
+    const int hand_to = 5 + quad * 2 + part;          // barrier this part arrives on
+    const int hand_from = 5 + quad * 2 + (part ^ 1);  // barrier this part waits on
+    float* hand_out = hand + part * 2 * kRowsPerTile;
+    const float* hand_in = hand + (part ^ 1) * 2 * kRowsPerTile;
+    for (int64_t g = part; g < NG; g += 2) {
+      const int64_t n = nP + g;
+      uint32_t tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(n & 1);
+      if (ok && !wait_scores(n, tS)) ok = false;
+      uint32_t sv[kGroup];
+      if (live) tmem_ld<kGroup>(tS, sv);
       tmem_wait_ld();
-    }
-    for (int64_t n = nP; n < total && ok; ++n) {
-      uint32_t tS;
-      if (!wait_scores(n, tS)) { ok = false; break; }
-      {
-        // ---------------- Phase 2: group g ----------------
-        const int64_t g = n - nP;
-        uint32_t pk[kGC / 2];
-        uint32_t upk[DQ / 2];
-        uint32_t sv[kGC];
-        if (live) tmem_ld<kGC>(tS + part * kGC, sv);
-        tmem_wait_ld();
-        // the scores are in registers: the S buffer may take the scores of step n + 2
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[n & 1]);
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(24, n);
-        if (live) {
-          // columns of selected blocks or of blocks >= NT are masked (:228)
-          const int jb0 = int(g) * kGroup + part * kGC;  // NT <= kMaxNT fits in int
-          const int lim = int(NT) - jb0;
-          const uint32_t word = maskw[half * kMaxNG + g] >> (part * kGC);
+      // the scores are in registers: the S buffer may take the scores of step n + 2
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s2_free[part]);
+      uint32_t pk[kGroup / 2];
+      float w = 0.f;
+      if (live) {  // uniform per lane quadrant: both parts of a quadrant take this branch
+        // columns of selected blocks or of blocks >= NT are masked (:228)
+        const int jb0 = int(g) * kGroup;  // NT <= kMaxNT fits in int
+        const int lim = int(NT) - jb0;
+        const uint32_t word = maskw[half * kMaxNG + g];
 #pragma unroll
-          for (int c = 0; c < kGC; ++c)
-            if (c >= lim || ((word >> c) & 1u)) sv[c] = __float_as_uint(-INFINITY);
-          float mx = max_tree<kGC>(sv);
-          if (warp == 3 && lane == 0) PASA_TRACE_MARK(23, n);
-          mx = row_reduce(mx, true);
-          if (warp == 3 && lane == 0) PASA_TRACE_MARK(25, n);
-          mx = (mx == -INFINITY) ? mx : mx * sm_scale;
-          const float m_true_new = fmaxf(m_true, mx);
-          const bool grow = mx > m_used + kRescaleThresh;  // m_used is finite for live rows here
-          const float alpha = grow ? fast_exp2(m_used - mx) : 1.0f;
-          if (__any_sync(0xffffffffu, grow)) {
-            if (!rescale_o(n, alpha)) ok = false;
-          }
-          l1 *= alpha;
-          if (grow) m_used = mx;
-          float p[kGC];
-          const float negm = -m_used;
-#pragma unroll
-          for (int c = 0; c < kGC; ++c) p[c] = exp2_ftz(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
-          if (warp == 3 && lane == 0) PASA_TRACE_MARK(26, n);
-          float psum = 0.f, wsum;
-          {
-            float a0 = 0.f, a1 = 0.f, extra = 0.f;
-            // bit of the ragged last block's column, if it is one of this thread's
-            // (a bit test, not an index: p[] must stay in registers)
-            const uint32_t lastbit = (lim >= 1 && lim <= kGC) ? (1u << (lim - 1)) : 0u;
-#pragma unroll
-            for (int c = 0; c < kGC; c += 2) {
-              a0 += p[c]; a1 += p[c + 1];
-              extra += ((lastbit >> c) & 1u) ? p[c] : (((lastbit >> (c + 1)) & 1u) ? p[c + 1] : 0.f);
-            }
-            psum = a0 + a1;
-            // the ragged last block has its own length (:220)
-            wsum = psum * float(kBlock) + extra * float(last_len - kBlock);
-          }
-#pragma unroll
-          for (int c = 0; c < kGC; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
-          psum = row_reduce(psum, false);
-          if (warp == 3 && lane == 0) PASA_TRACE_MARK(27, n);
-          // the reference's probabilities use the exact running max (:237, :243)
-          gl += wsum * fast_exp2(m_used - m_true_new);
-          m_true = m_true_new;
-          const float w = psum * scale32;  // :253
-#pragma unroll
-          for (int x = 0; x < DQ / 2; ++x) {
-            const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qpk[x]));
-            upk[x] = pack_bf16x2(qf.x * w, qf.y * w);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kGC / 2; ++c) pk[c] = 0u;
-#pragma unroll
-          for (int x = 0; x < DQ / 2; ++x) upk[x] = 0u;
+        for (int c = 0; c < kGroup; ++c)
+          if (c >= lim || ((word >> c) & 1u)) sv[c] = __float_as_uint(-INFINITY);
+        float mx = max_tree<kGroup>(sv);
+        mx = (mx == -INFINITY) ? mx : mx * sm_scale;
+        if (g >= 1) {  // running maxima after group g - 1
+          named_bar_sync(hand_from, 64);
+          m_used = hand_in[r];
+          m_true = hand_in[kRowsPerTile + r];
         }
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(20, n);
-        if (!wait_p_free(n)) ok = false;
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(21, n);
-        tmem_st<kGC / 2>(tP + 16u * uint32_t(n & 1) + part * (kGC / 2), pk);
-        tmem_st<DQ / 2>(tmem + lane_base + C::kColS0 + 128u * uint32_t((n + 1) & 1) + C::kColU + part * (DQ / 2),
-                        upk);
-        tmem_wait_st();
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(22, n);
+        const float m_used_prev = m_used;
+        const float m_true_new = fmaxf(m_true, mx);
+        const bool grow = mx > m_used + kRescaleThresh;  // m_used is finite for live rows here
+        if (grow) m_used = mx;
+        if (g + 1 < NG) {
+          hand_out[r] = m_used;
+          hand_out[kRowsPerTile + r] = m_true_new;
+          named_bar_arrive(hand_to, 64);
+        }
+        if (__any_sync(0xffffffffu, grow)) {  // O holds steps <= n-1 in units of m_used_prev
+          const float alpha = grow ? fast_exp2(m_used_prev - m_used) : 1.0f;
+          if (ok && !rescale_o_all(n, alpha)) ok = false;
+        }
+        if (m_applied != m_used) { l1 *= fast_exp2(m_applied - m_used); m_applied = m_used; }
+        float p[kGroup];
+        const float negm = -m_used;
+#pragma unroll
+        for (int c = 0; c < kGroup; ++c) p[c] = exp2_ftz(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
+        float psum, wsum;
+        {
+          float a0 = 0.f, a1 = 0.f, extra = 0.f;
+          // bit of the ragged last block's column, if it is in this group
+          // (a bit test, not an index: p[] must stay in registers)
+          const uint32_t lastbit = (lim >= 1 && lim <= kGroup) ? (1u << (lim - 1)) : 0u;
+#pragma unroll
+          for (int c = 0; c < kGroup; c += 2) {
+            a0 += p[c]; a1 += p[c + 1];
+            extra += ((lastbit >> c) & 1u) ? p[c] : (((lastbit >> (c + 1)) & 1u) ? p[c + 1] : 0.f);
+          }
+          psum = a0 + a1;
+          // the ragged last block has its own length (:220)
+          wsum = psum * float(kBlock) + extra * float(last_len - kBlock);
+        }
+#pragma unroll
+        for (int c = 0; c < kGroup; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
+        // the reference's probabilities use the exact running max (:237, :243)
+        gl += wsum * fast_exp2(m_used - m_true_new);
+        m_true = m_true_new;
+        w = psum * scale32;  // :253
+      } else {
+#pragma unroll
+        for (int c = 0; c < kGroup / 2; ++c) pk[c] = 0u;
       }
-      release_step(n);
+      if (ok && !wait_p_free(n)) ok = false;
+      tmem_st<kGroup / 2>(tP + 16u * uint32_t(n & 1), pk);
+      // U = bf16(w q) over all D columns, 32 packed columns at a time (Q read back from TMEM)
+      const uint32_t tU = tmem + lane_base + C::kColS0 + 128u * uint32_t((n + 1) & 1) + C::kColU;
+#pragma unroll
+      for (int c0 = 0; c0 < D / 2; c0 += 32) {
+        uint32_t qv[32];
+        tmem_ld32(tmem + lane_base + C::kColQ + c0, qv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qv[x]));
+          qv[x] = pack_bf16x2(qf.x * w, qf.y * w);
+        }
+        tmem_st32(tU + c0, qv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && warp < 11) PASA_TRACE_MARK(12 + (warp - 3), n);
+      if (lane == 0) mbar_arrive(&p2_ready[part]);
+    }
+    // Each part ends with the maxima of the last group it saw; the maxima only
+    // grow, so the larger pair is the final one.
+    if (live) {
+      m_used = row_reduce(m_used, true);
+      m_true = row_reduce(m_true, true);
+      if (m_applied != m_used) l1 *= fast_exp2(m_applied - m_used);
     }
 
     // ---------------- Final: o = O / (l + g_l) ----------------
@@ -707,10 +769,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       }
     }
     if (!ok) report(P.err);
+    if (warp == 3 && lane == 0) PASA_TRACE_CTL(2);
   }
 
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) PASA_TRACE_CTL(3);
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
@@ -781,5 +845,12 @@ cudaError_t launch_attn_tc(cudaStream_t st, int D, const void* q, const void* k,
 #ifdef PASA_TRACE
 extern "C" PASA_API int pasa_trace_read(void* host_dst, size_t bytes) {
   return cudaMemcpyFromSymbol(host_dst, pasa::tc::g_pasa_trace, bytes) == cudaSuccess ? 0 : PASA_ERR_CUDA;
+}
+extern "C" PASA_API int pasa_trace_ctl_read(void* host_dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(host_dst, pasa::tc::g_pasa_trace_ctl, bytes) == cudaSuccess ? 0 : PASA_ERR_CUDA;
+}
+extern "C" PASA_API int pasa_trace_select(unsigned int x, unsigned int y) {
+  const unsigned int v[2] = {x, y};
+  return cudaMemcpyToSymbol(pasa::tc::g_pasa_trace_cta, v, sizeof(v)) == cudaSuccess ? 0 : PASA_ERR_CUDA;
 }
 #endif

@@ -334,6 +334,11 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
 }
+// Arrive on a named barrier without waiting (the producer side of a
+// producer/consumer hand-off; the consumer uses named_bar_sync).
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
