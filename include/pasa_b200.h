@@ -165,6 +165,31 @@ PASA_API int pasa_forward_noalloc(void* stream, const void* q, const void* k, co
                  void* o, int kernel);
 
 /*
+ * The whole op on HOST memory: q, k, v and o are [B, H, T, D] host buffers.
+ * This entry point has no counterpart in the reference (whose op takes
+ * device tensors); it serves callers whose activations live on the host.
+ * The heads are split into chunks of heads_per_chunk; chunk i is computed
+ * (a pasa_forward call on its heads) while chunk i+1 is copied in and chunk
+ * i-1 copied out, on three streams owned by the library.  The result is the
+ * one pasa_forward gives on the same heads.
+ *   - The call is synchronous: it returns when o holds the result.  Work
+ *     queued on `stream` before the call is ordered before it.
+ *   - The copies overlap the compute only when the host buffers are
+ *     page-locked (cudaHostAlloc / cudaHostRegister).
+ *   - workspace: device memory of pasa_forward_host_workspace_size() bytes,
+ *     256-byte aligned, not used by anything else during the call.
+ *   - noise_h: NULL, or host [B*H, NT] floats as in pasa_select.
+ *   - err_bits (nullable, host): the OR of the chunks' PASA_DEVERR_* bits.
+ */
+PASA_API int pasa_forward_host_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype,
+                 double density, int64_t heads_per_chunk, size_t* bytes);
+PASA_API int pasa_forward_host(void* stream, const void* q_h, const void* k_h, const void* v_h,
+                 int64_t B, int64_t H, int64_t T, int D, int dtype,
+                 double density, float scale, int use_cov_bias, const float* noise_h,
+                 void* workspace, size_t workspace_bytes, int64_t heads_per_chunk,
+                 void* o_h, uint32_t* err_bits, int kernel);
+
+/*
  * Token-layout permutation of the temporal heads (frame-major <-> token-
  * major), text tail untouched.  Replaces hunyuan_sparse_head_placement
  * (svg/models/hyvideo/placement.py:34-153) when inverse = 0 and

@@ -10,10 +10,12 @@ from .ops import (  # noqa: F401
     hunyuan_sparse_head_placement,
     piecewise_sparse_attention,
     pisa_pg_attention,
+    pisa_pg_attention_host,
 )
 
 __all__ = [
     "pisa_pg_attention",
+    "pisa_pg_attention_host",
     "piecewise_sparse_attention",
     "hunyuan_sparse_head_placement",
     "hunyuan_hidden_states_placement",

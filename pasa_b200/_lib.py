@@ -36,6 +36,7 @@ DEVERR_WAIT_TIMEOUT = 0x1
 EXPORTS = (
     "pasa_abi_version", "pasa_status_string", "pasa_derive", "pasa_workspace_size", "pasa_prep",
     "pasa_select", "pasa_attn", "pasa_forward", "pasa_forward_noalloc", "pasa_place",
+    "pasa_forward_host_workspace_size", "pasa_forward_host",
 )
 
 _lib = None
@@ -68,6 +69,10 @@ def load() -> ctypes.CDLL:
                                c_int]),
         "pasa_forward_noalloc": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float,
                                          c_int, P, P, c_int]),
+        "pasa_forward_host_workspace_size": (c_int, [c_int64, c_int64, c_int64, c_int, c_int, c_double, c_int64,
+                                                     POINTER(c_size_t)]),
+        "pasa_forward_host": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float, c_int,
+                                      P, P, c_size_t, c_int64, P, POINTER(c_uint32), c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -8,6 +8,8 @@ stream and the random draw of ``use_random``; there is no CPU or Triton path.
 """
 from __future__ import annotations
 
+import ctypes
+
 from typing import Optional
 
 import torch
@@ -183,6 +185,65 @@ def pisa_pg_attention(
             float(scale), int(bool(use_cov_bias)), _ptr(noise), ws.data_ptr(), ws_bytes, o.data_ptr(),
             int(kernel)))
     return o
+
+
+def pisa_pg_attention_host(
+    q, k, v,
+    density=0.15,
+    scale=None,
+    use_cov_bias=True,
+    use_random=False,
+    *,
+    heads_per_chunk: int = 4,
+    out: Optional[torch.Tensor] = None,
+    device=None,
+    kernel: int = _lib.ATTN_AUTO,
+):
+    """The same op on host-resident tensors: q, k, v are [B, H, T, D] CPU
+    tensors (page-locked for the copies to overlap the compute) and the
+    result is a CPU tensor like ``v`` (``out`` if given).  The heads go
+    through the GPU in chunks of ``heads_per_chunk``: chunk i is computed
+    while chunk i+1 is copied in and chunk i-1 copied out
+    (``pasa_forward_host``).  No counterpart in the reference, whose op takes
+    CUDA tensors; the result equals ``pisa_pg_attention`` on the same heads.
+    Synchronous: returns when the result is in host memory.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu":
+            raise ValueError(f"{name} must be a CPU tensor")
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be [B, H, T, D]")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k and v must have the same shape")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k and v must have the same dtype")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, T, K = q.shape
+    dcode = _dtype_code(q)
+    scale = K ** -0.5 if scale is None else scale
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    NT, NG, NS = _lib.derive(T, density)
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    elif out.shape != q.shape or out.dtype != q.dtype or out.device.type != "cpu" or not out.is_contiguous():
+        raise ValueError("out must be a contiguous CPU tensor like q")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        noise = None
+        if use_cov_bias and use_random:
+            noise = torch.randn((B, H, NT), dtype=torch.float32, device=dev).cpu()
+        n = ctypes.c_size_t()
+        _lib.check("pasa_forward_host_workspace_size", lib.pasa_forward_host_workspace_size(
+            B, H, T, K, dcode, float(density), int(heads_per_chunk), ctypes.byref(n)))
+        ws = torch.empty(n.value, dtype=torch.uint8, device=dev)
+        err = ctypes.c_uint32(0)
+        _lib.check("pasa_forward_host", lib.pasa_forward_host(
+            _stream_ptr(dev), q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, T, K, dcode, float(density),
+            float(scale), int(bool(use_cov_bias)), _ptr(noise), ws.data_ptr(), n.value, int(heads_per_chunk),
+            out.data_ptr(), ctypes.byref(err), int(kernel)))
+    if err.value & _lib.DEVERR_WAIT_TIMEOUT:
+        raise RuntimeError("pasa_forward_host: a kernel gave up waiting on a barrier (device error word)")
+    return out
 
 
 def piecewise_sparse_attention(q, k, v, density=0.15, block_size=64, use_random=False, **kwargs):
