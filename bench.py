@@ -38,9 +38,9 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per launch of the attention kernel from one ncu
-# capture of 4 of the 40 heads, scaled by 10 (work and bytes are per head):
-# profiles/attn_tc_wan14b_720p.md.  Keyed by (workload, kernel).
-ATTN_TRAFFIC_BYTES = {("wan14b-720p", "tcgen05"): 3.145e9}
+# capture of 4 of the 40 heads (237.4 MB read + 61.3 MB written), scaled by
+# 10 (work and bytes are per head).  Keyed by (workload, kernel).
+ATTN_TRAFFIC_BYTES = {("wan14b-720p", "tcgen05"): 2.987e9}
 
 
 def parse():
