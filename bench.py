@@ -333,18 +333,41 @@ def main():
     peak_tf = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
     F_rank = w.exact_flops(nh)
     achieved = F_rank / (attn_ms * 1e-3) / 1e12
-    traffic = ATTN_TRAFFIC_BYTES.get((w.name, args.kernel if args.kernel != "auto" else "tcgen05"))
+    traffic = ATTN_TRAFFIC_BYTES.get((w.name, "tcgen05" if resolved == _lib.ATTN_TCGEN05 else "simt"))
     if traffic is not None:
         full = synth.WORKLOADS[args.config].heads
         traffic = traffic * nh / full  # this rank's launch covers nh of the workload's heads
+    # MMA work the tensor-core kernel executes on this call's selections: a CTA
+    # serves query blocks 2p and 2p+1 and takes ceil(|S_2p ∪ S_2p+1| / 2)
+    # steps of two key blocks (score and P.V MMAs, M=128, N=K=128), then one
+    # step per 32-block group (scores N=32, P_g.vc_g K=32, U.H_g K=D)
+    exec_flop = None
+    resolved = kernel if kernel != _lib.ATTN_AUTO else (
+        _lib.ATTN_TCGEN05 if q.dtype == torch.bfloat16 else _lib.ATTN_SIMT)  # as pasa_attn resolves AUTO
+    if resolved == _lib.ATTN_TCGEN05:
+        m = st.sel_mask.view(torch.int32)
+        a, b = m[:, 0::2], m[:, 1::2]
+        if b.shape[1] < a.shape[1]:
+            b = torch.cat([b, torch.zeros_like(a[:, :1])], 1)
+        union = torch.bitwise_or(a, b)
+        bits = sum(((union >> i) & 1).sum(-1) for i in range(32))          # [BH, pairs]
+        steps1 = int(((bits + 1) // 2).sum())
+        tiles = int(a.shape[0] * a.shape[1])
+        exec_flop = steps1 * 4 * 128 * 128 * D + tiles * NG * (4 * 128 * 32 * D + 2 * 128 * D * D)
     roofline = {
-        "kernel": "attn_tc_kernel<128>" if kernel != _lib.ATTN_SIMT else "attn_simt_kernel",
+        "kernel": f"attn_tc_kernel<{D}>" if resolved == _lib.ATTN_TCGEN05 else f"attn_simt_kernel<{D}>",
         "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
         "frac": achieved / peak_tf, "traffic": traffic,
         "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
         "achieved_basis": "exact-block FLOPs per launch / mean CUDA-event launch time",
         "achieved_incl_correction": (w.exact_flops(nh) + w.corr_flops(nh)) / (attn_ms * 1e-3) / 1e12,
     }
+    if exec_flop is not None:
+        # the MMAs the kernel runs (union of two query blocks' selections per
+        # tile, plus the correction): how busy the tensor core is kept
+        roofline["executed_tflop"] = exec_flop / 1e12
+        roofline["achieved_executed"] = exec_flop / (attn_ms * 1e-3) / 1e12
+        roofline["frac_executed"] = roofline["achieved_executed"] / peak_tf
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
