@@ -333,6 +333,8 @@ def main():
     peak_tf = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
     F_rank = w.exact_flops(nh)
     achieved = F_rank / (attn_ms * 1e-3) / 1e12
+    resolved = kernel if kernel != _lib.ATTN_AUTO else (
+        _lib.ATTN_TCGEN05 if q.dtype == torch.bfloat16 else _lib.ATTN_SIMT)  # as pasa_attn resolves AUTO
     traffic = ATTN_TRAFFIC_BYTES.get((w.name, "tcgen05" if resolved == _lib.ATTN_TCGEN05 else "simt"))
     if traffic is not None:
         full = synth.WORKLOADS[args.config].heads
@@ -342,8 +344,6 @@ def main():
     # steps of two key blocks (score and P.V MMAs, M=128, N=K=128), then one
     # step per 32-block group (scores N=32, P_g.vc_g K=32, U.H_g K=D)
     exec_flop = None
-    resolved = kernel if kernel != _lib.ATTN_AUTO else (
-        _lib.ATTN_TCGEN05 if q.dtype == torch.bfloat16 else _lib.ATTN_SIMT)  # as pasa_attn resolves AUTO
     if resolved == _lib.ATTN_TCGEN05:
         m = st.sel_mask.view(torch.int32)
         a, b = m[:, 0::2], m[:, 1::2]
