@@ -128,6 +128,19 @@ PASA_API int pasa_attn(void* stream, const void* q, const void* k, const void* v
               void* o, uint32_t* err_word, int kernel);
 
 /*
+ * Dense attention o = softmax(q k^T scale) v on the tensor-core kernel, for
+ * the layers and timesteps the models run dense (the `full_attention_flag`
+ * branch of attention_core_logic, svg/models/wan/attention.py:364-383 and
+ * svg/models/hyvideo/attention.py:666-672, which calls SDPA / FlashInfer).
+ * It is pisa_pg_attention with every block selected (density 1) without the
+ * block statistics, the selection and the correction, whose terms are then
+ * exactly zero.  q, k, v, o: [BH, T, D] bf16.
+ */
+PASA_API int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v,
+              int64_t BH, int64_t T, int D, int dtype, float scale,
+              void* o, uint32_t* err_word);
+
+/*
  * The whole op, pisa_pg_attention(q, k, v, density, ..., scale,
  * use_cov_bias) (group_pisa_attention.py:307-398) on caller memory:
  * prep -> select -> attention on `stream`.  workspace must hold

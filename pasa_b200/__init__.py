@@ -6,6 +6,7 @@ placement (svg/models/hyvideo/placement.py), running hand-written CUDA
 through the C ABI in ``include/pasa_b200.h``.
 """
 from .ops import (  # noqa: F401
+    dense_attention,
     hunyuan_hidden_states_placement,
     hunyuan_sparse_head_placement,
     piecewise_sparse_attention,
@@ -14,6 +15,7 @@ from .ops import (  # noqa: F401
 )
 
 __all__ = [
+    "dense_attention",
     "pisa_pg_attention",
     "pisa_pg_attention_host",
     "piecewise_sparse_attention",

@@ -36,7 +36,7 @@ DEVERR_WAIT_TIMEOUT = 0x1
 EXPORTS = (
     "pasa_abi_version", "pasa_status_string", "pasa_derive", "pasa_workspace_size", "pasa_prep",
     "pasa_select", "pasa_attn", "pasa_forward", "pasa_forward_noalloc", "pasa_place",
-    "pasa_forward_host_workspace_size", "pasa_forward_host",
+    "pasa_forward_host_workspace_size", "pasa_forward_host", "pasa_dense_attn",
 )
 
 _lib = None
@@ -73,6 +73,7 @@ def load() -> ctypes.CDLL:
                                                      POINTER(c_size_t)]),
         "pasa_forward_host": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float, c_int,
                                       P, P, c_size_t, c_int64, P, POINTER(c_uint32), c_int]),
+        "pasa_dense_attn": (c_int, [P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

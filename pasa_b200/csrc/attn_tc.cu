@@ -112,6 +112,7 @@ struct Params {
   __nv_bfloat16* o;
   const uint32_t* sel_mask;
   uint32_t* err;
+  int dense;  // every key block selected for every query block (sel_mask unused, no phase 2)
 };
 
 // Optional step tracer (compile with -DPASA_TRACE): one CTA, chosen with
@@ -200,8 +201,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     prefetch_tmap(&maps.kc); prefetch_tmap(&maps.vc); prefetch_tmap(&maps.h);
   }
   for (int64_t w = tid; w < NG; w += kThreads) {
-    maskw[w] = P.sel_mask[(bh * NT + blkA) * NG + w];
-    maskw[kMaxNG + w] = hasB ? P.sel_mask[(bh * NT + blkB) * NG + w] : 0u;
+    if (P.dense) {  // all blocks < NT
+      const int64_t left = NT - w * 32;
+      const uint32_t all = left >= 32 ? 0xFFFFFFFFu : ((1u << left) - 1u);
+      maskw[w] = all;
+      maskw[kMaxNG + w] = hasB ? all : 0u;
+    } else {
+      maskw[w] = P.sel_mask[(bh * NT + blkA) * NG + w];
+      maskw[kMaxNG + w] = hasB ? P.sel_mask[(bh * NT + blkB) * NG + w] : 0u;
+    }
   }
   __syncthreads();
   if (warp == 0) {
@@ -270,7 +278,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   if (tid == 0) PASA_TRACE_CTL(1);
   const int64_t nU = s_nu;
   const int64_t nP = (nU + 1) / 2;  // phase-1 steps: two union blocks each (a lone last block pairs with itself)
-  const int64_t total = nP + NG;
+  // phase 2 corrects the blocks a query block did not select; with every
+  // block selected (dense) there are none and its terms are exactly zero
+  const int64_t NG2 = P.dense ? 0 : NG;
+  const int64_t total = nP + NG2;
 
 
   if (warp == 0) {
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         if (!mbar_wait_bounded(&empty_v[p % C::kSV], uint32_t((p / C::kSV) & 1), kPollLimit)) ok = false;
       // Phase 2: kc, vc rows and H of every group through ring 2
       int64_t issued2 = 0;
-      for (int64_t g = 0; g < NG && ok; ++g) {
+      for (int64_t g = 0; g < NG2 && ok; ++g) {
         const int s = int(g % C::kS2);
         if (!mbar_wait_bounded(&empty2[s], uint32_t((g / C::kS2) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
         PASA_TRACE_MARK(0, nP + g);
@@ -739,7 +750,7 @@ bool make_map(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t bat
 template <int D>
 cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const void* v, const void* kc,
                         const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
-                        float scale, void* o, uint32_t* err) {
+                        float scale, void* o, uint32_t* err, int dense) {
   using C = Cfg<D>;
   const int64_t NT = cdiv(T_len, kBlock), NG = cdiv(NT, kGroup), NTP = NG * kGroup;
   if (NT > kMaxNT) return cudaErrorInvalidValue;
@@ -750,7 +761,7 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
     return cudaErrorInvalidValue;
   Params p;
   p.T = T_len; p.NT = NT; p.NG = NG; p.NTP = NTP; p.scale = scale;
-  p.o = static_cast<__nv_bfloat16*>(o); p.sel_mask = mask; p.err = err;
+  p.o = static_cast<__nv_bfloat16*>(o); p.sel_mask = mask; p.err = err; p.dense = dense;
   auto kern = attn_tc_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -763,9 +774,9 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
 
 cudaError_t launch_attn_tc(cudaStream_t st, int D, const void* q, const void* k, const void* v, const void* kc,
                            const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
-                           int64_t /*NS*/, float scale, void* o, uint32_t* err) {
-  if (D == 64) return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err);
-  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err);
+                           int64_t /*NS*/, float scale, void* o, uint32_t* err, int dense) {
+  if (D == 64) return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense);
+  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense);
 }
 
 }  // namespace pasa

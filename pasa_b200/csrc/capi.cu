@@ -16,7 +16,7 @@ cudaError_t launch_attn_simt(cudaStream_t, int, int, const void*, const void*, c
                              const void*, const void*, const int32_t*, const uint32_t*, int64_t, int64_t,
                              int64_t, float, void*);
 cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const void*, const void*, const void*,
-                           const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*);
+                           const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*, int);
 cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
                          int64_t, int64_t, int64_t, int);
 }  // namespace pasa
@@ -160,7 +160,7 @@ int pasa_attn(void* stream, const void* q, const void* k, const void* v, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (kernel == PASA_ATTN_TCGEN05) {
     if (dtype != PASA_BF16) return PASA_ERR_DTYPE;
-    return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word));
+    return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word, 0));
   }
   if (kernel != PASA_ATTN_SIMT) return PASA_ERR_UNSUPPORTED;
   if (!indices) return PASA_ERR_NULL;
@@ -199,6 +199,20 @@ int pasa_forward(void* stream, const void* q, const void* k, const void* v, int6
     return st;
   if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
   return pasa_attn(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel);
+}
+
+int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, int64_t BH, int64_t T, int D,
+                    int dtype, float scale, void* o, uint32_t* err_word) {
+  int st = check_common(BH, T, D, dtype);
+  if (st) return st;
+  if (dtype != PASA_BF16) return PASA_ERR_DTYPE;  // the tensor-core kernel runs bf16
+  if (!q || !k || !v || !o) return PASA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return PASA_ERR_ALIGN;
+  if (!std::isfinite(scale)) return PASA_ERR_SHAPE;
+  if ((st = check_device())) return st;
+  // the block statistics are not read in dense mode; q stands in for their (unused) tensor maps
+  return cuda_status(launch_attn_tc(static_cast<cudaStream_t>(stream), D, q, k, v, q, q, q, nullptr, BH, T,
+                                    cdiv(T, kBlock), scale, o, err_word, 1));
 }
 
 int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal, int64_t cfg, int64_t H,

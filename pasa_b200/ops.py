@@ -246,6 +246,28 @@ def pisa_pg_attention_host(
     return out
 
 
+def dense_attention(q, k, v, scale=None):
+    """Dense attention softmax(q k^T scale) v for [B, H, T, D] bf16 CUDA tensors
+    on the tensor-core kernel (pasa_dense_attn): the branch the models take for
+    their dense layers and timesteps (SDPA in the reference,
+    svg/models/wan/attention.py:299-301).  Returns a new tensor like ``v``.
+    """
+    _check_qkv(q, k, v)
+    if q.dtype != torch.bfloat16:
+        raise ValueError("dense_attention runs the bf16 tensor-core kernel; q, k, v must be bf16")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, T, K = q.shape
+    scale = K ** -0.5 if scale is None else scale
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        o = torch.empty_like(v)
+        err = torch.zeros(1, dtype=torch.int32, device=q.device)
+        _lib.check("pasa_dense_attn", lib.pasa_dense_attn(
+            _stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), B * H, T, K, _dtype_code(q),
+            float(scale), o.data_ptr(), err.data_ptr()))
+    return o
+
+
 def piecewise_sparse_attention(q, k, v, density=0.15, block_size=64, use_random=False, **kwargs):
     """The name the model processors call (svg/models/wan/attention.py:384,
     svg/models/hyvideo/attention.py:640, :682); its source is not in the
