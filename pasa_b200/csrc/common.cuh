@@ -32,6 +32,21 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ void store(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
 };
 
+// fp32 -> bf16 -> fp32 with round-to-nearest-even, on the integer pipe: add
+// half an ulp of bf16 (0x7FFF, plus the kept bit's parity for ties) to the
+// bit pattern and clear the low 16 bits.  Equals the conversion instruction
+// for every finite input (subnormals included); inputs here are finite sums.
+__device__ __forceinline__ float round_bf16_int(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return __uint_as_float((b + 0x7FFFu + ((b >> 16) & 1u)) & 0xFFFF0000u);
+}
+// Two roundings with one packed conversion (cvt.rn.bf16x2.f32).
+__device__ __forceinline__ void round_bf16_pair(float& lo, float& hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  lo = __low2float(h);
+  hi = __high2float(h);
+}
+
 // 2^x with the hardware approximation (ex2.approx.f32), the instruction the
 // reference's tl.math.exp2 lowers to.
 __device__ __forceinline__ float fast_exp2(float x) {

@@ -59,7 +59,8 @@ __device__ __forceinline__ void load_block(__nv_bfloat16* stage, const __nv_bflo
   }
 }
 
-// halving-tree column sum in bf16 (each partial sum rounded), as prep.cu
+// halving-tree column sum in bf16 (each partial sum rounded), as prep.cu;
+// the roundings alternate between the packed conversion and the integer pipe
 template <int D>
 __device__ __forceinline__ float tree_sum(const __nv_bfloat16* tile, int c) {
   using C = Cfg<D>;
@@ -67,11 +68,16 @@ __device__ __forceinline__ float tree_sum(const __nv_bfloat16* tile, int c) {
 #pragma unroll
   for (int r = 0; r < kBlock; ++r) x[r] = __bfloat162float(tile[r * C::kRS + c]);
 #pragma unroll
-  for (int n = kBlock; n > 1; n >>= 1) {
+  for (int n = kBlock; n > 2; n >>= 1) {  // every level but the last has an even count: packed roundings
 #pragma unroll
-    for (int r = 0; r < n / 2; ++r) x[r] = Elem<__nv_bfloat16>::round(x[r] + x[r + n / 2]);
+    for (int r = 0; r < n / 2; r += 2) {
+      float a = x[r] + x[r + n / 2], b = x[r + 1] + x[r + 1 + n / 2];
+      round_bf16_pair(a, b);
+      x[r] = a;
+      x[r + 1] = b;
+    }
   }
-  return x[0];
+  return round_bf16_int(x[0] + x[1]);
 }
 
 template <int D>
@@ -190,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
           const int b = bn + ni * 8 + 2 * tq + (e & 1);
           const float hc = fmaf(-kc_f[a], vc_f[b], acc[mi][ni][e]);  // :106-107
           nsq = fmaf(hc, hc, nsq);                                     // :110
-          gsum[mi][ni][e] += Elem<__nv_bfloat16>::round(hc);          // hc stored in v dtype (:125)
+          gsum[mi][ni][e] += round_bf16_int(hc);                      // hc stored in v dtype (:125)
         }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) nsq += __shfl_xor_sync(0xffffffffu, nsq, off);
