@@ -55,6 +55,12 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tcgen05", "simt"])
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads (small profiling cases)")
+    ap.add_argument("--dit", action="store_true",
+                    help="time the full Wan2.1-14B DiT denoising step (PASA in every layer, Ulysses over ranks)")
+    ap.add_argument("--dit-layers", type=int, default=40, help="blocks in the DiT step (40 = the full model)")
+    ap.add_argument("--dit-density", type=float, default=0.1)
+    ap.add_argument("--dit-torch", action="store_true",
+                    help="DiT step with torch elementwise ops instead of the row kernels (comparison)")
     return ap.parse_args()
 
 
@@ -218,8 +224,144 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_dit(args):
+    """One denoising step of the Wan2.1-14B DiT at 720p (81 frames -> 21 x 45 x
+    80 = 75600 tokens): patch embedding, 40 blocks with PASA self-attention,
+    output head.  With N ranks every rank holds 75600/N tokens and the self-
+    attention reshards sequence <-> heads with NCCL all-to-alls (Ulysses)."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+
+    from pasa_b200 import dit, ops
+
+    world, rank, local = init_dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = dataclasses.replace(dit.WAN14B_720P, layers=args.dit_layers, density=args.dit_density)
+    if cfg.heads % world:
+        raise SystemExit(f"{cfg.heads} heads do not split over {world} ranks")
+    group = dist.group.WORLD if world > 1 else None
+    t0, t1 = dit.local_slice(cfg, rank, world)
+    stream = torch.cuda.current_stream(dev)
+
+    # identical weights and inputs on every rank (same seeds); latents and text on the host
+    blocks = [dit.init_block(cfg, 1000 + i, dev) for i in range(cfg.layers)]
+    embed = dit.init_embed(cfg, 999, dev)
+    g = torch.Generator().manual_seed(0)
+    lat = torch.randn((1, cfg.in_channels, cfg.frames, 2 * cfg.height, 2 * cfg.width), generator=g)
+    text_h = torch.randn((1, cfg.text_len, cfg.text_dim), generator=g).to(torch.bfloat16).pin_memory()
+    lat_h = dit.patchify(lat)[:, t0:t1].to(torch.bfloat16).contiguous().pin_memory()
+    out_h = torch.empty((1, t1 - t0, cfg.in_channels * 4), dtype=torch.bfloat16).pin_memory()
+    cos, sin = dit.rope_table(cfg, dev)
+    rope = (cos[t0:t1].contiguous(), sin[t0:t1].contiguous())
+    timestep = torch.tensor([900], device=dev)
+    lat_d, text_d = lat_h.to(dev), text_h.to(dev)
+
+    attn_events = []
+
+    def core(q, k, v):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        o = ops.pisa_pg_attention(q, k, v, density=cfg.density)
+        e1.record(stream)
+        attn_events.append((e0, e1))
+        return o
+
+    fused = not args.dit_torch
+
+    def step():
+        return dit.step(lat_d, timestep, text_d, rope, embed, blocks, cfg, core, group, fused=fused)
+
+    def e2e_step():
+        # the public call with host buffers: latents and text in, predicted patches out
+        lat_g = lat_h.to(dev, non_blocking=True)
+        text_g = text_h.to(dev, non_blocking=True)
+        out = dit.step(lat_g, timestep, text_g, rope, embed, blocks, cfg, core, group, fused=fused)
+        out_h.copy_(out, non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        attn_events.clear()
+        gpu_ids = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
+        sampler = ClockSampler([gpu_ids[local] if local < len(gpu_ids) else local])
+        with sampler:
+            time.sleep(0.3)
+            barrier(world)
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for _ in range(args.steps):
+                out = step()
+            end.record(stream)
+            torch.cuda.synchronize()
+            barrier(world)
+        assert torch.isfinite(out).all()
+        ms_step = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+        attn_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in attn_events) / args.steps, world)
+        attn_events.clear()
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(s0.elapsed_time(s1) / args.steps, world)
+        assert torch.isfinite(out_h.float()).all()
+
+    clocks = sampler.summary()
+    nbytes = lambda t: t.numel() * t.element_size()
+    tokens = cfg.tokens
+    C, Fd, Lt = cfg.hidden, cfg.ffn, cfg.text_len
+    # GEMM FLOPs of one step (all ranks): per block 4 self-attention and 2
+    # cross-attention C x C projections over the video tokens, 2 over the text,
+    # the FFN pair, and the cross-attention scores/values
+    gemm = cfg.layers * (2 * tokens * C * C * 6 + 2 * Lt * C * C * 2 + 2 * 2 * tokens * C * Fd
+                         + 4 * tokens * Lt * C)
+    if rank == 0:
+        line = {
+            "metric": "Wan2.1-14B DiT denoising step, PASA in every layer (ms per step)",
+            "value": ms_step, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents and text embeddings, random-init weights)",
+            "config": {"workload": "wan14b-720p-dit-step", "layers": cfg.layers, "hidden": C, "heads": cfg.heads,
+                       "ffn": Fd, "tokens": tokens, "text_len": Lt, "density": cfg.density,
+                       "parallelism": f"ulysses{world}" if world > 1 else "none",
+                       "elementwise": "row kernels (pasa_dit_row_norm, pasa_dit_qkv_rope)" if fused else "torch ops",
+                       "l2": "activations 0.77 GB per tensor > 126 MB L2; no flush"},
+            "kernels_ms": {"pasa_attention_per_step": attn_ms,
+                           "attention_share": attn_ms / ms_step},
+            "gemm_tflop_per_step": gemm / 1e12,
+            "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": (nbytes(lat_h) + nbytes(text_h)) * world,
+                    "d2h_bytes_per_step": nbytes(out_h) * world,
+                    "note": "dit.step from pinned host latents/text to pinned host output, per rank, summed over ranks"},
+            "clocks": clocks,
+            # per block: prep, select, attention, plus with the row kernels 3 norms
+            # and 3 producers (q/k/v, cross q, cross k); one more norm per step
+            "gpu_launches": ((9 * cfg.layers + 1) if fused else 3 * cfg.layers) * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.dit:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's DiT step needs diffusers and "
+                              "model checkpoints, neither present"}), flush=True)
+            return
+        run_dit(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

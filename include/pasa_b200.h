@@ -215,6 +215,62 @@ PASA_API int pasa_place(void* stream, const void* src, void* dst, const int32_t*
                int64_t cfg, int64_t H, int64_t T, int D, int dtype,
                int64_t context_length, int64_t num_frame, int64_t frame_size, int inverse);
 
+/*
+ * DiT row kernels around the attention op (bf16 activations, fp32 per-channel
+ * vectors, one 16-byte vector per element group: cols % 8 == 0, cols <= 8192,
+ * every pointer 16-byte aligned).
+ *
+ * Gated residual + LayerNorm / RMSNorm + affine + modulation in one pass.
+ * Replaces, for one row of cols elements, the reference's
+ * triton_modulate_gate_residual_forward (svg/kernels/triton/modulate.py:90-164),
+ * triton_layernorm_forward (layernorm.py:13-218), triton_modulate_shift_forward
+ * (modulate.py:12-85) and triton_rmsnorm_forward (rmsnorm.py:8-100), as the
+ * Wan block chains them (svg/models/wan/custom_models.py:38-111):
+ *   x' = add ? bf16(x + add * gate) : x        (gate NULL: plain add)
+ *   x_out = x'                                  (when add and x_out are given; may alias x)
+ *   y  = bf16(((x' - mean) * rstd) [* weight] [+ bias] [* (1 + scale) + shift])
+ * with rstd = 1 / sqrt(ssq / cols + eps) and, by `norm`:
+ *   PASA_DIT_RMSNORM           mean = 0, ssq = sum(x'^2)                (rmsnorm.py:31-35)
+ *   PASA_DIT_LAYERNORM         mean = sum(x') / cols, ssq = sum((x' - mean)^2)
+ *                              (the torch FP32LayerNorm the block runs without
+ *                              the fast kernels, custom_models.py:45)
+ *   PASA_DIT_LAYERNORM_PADDED  as LAYERNORM plus (P - cols) * mean^2, P = cols
+ *                              rounded up to a power of two: the reference's
+ *                              Triton LayerNorm sums its zero padding into the
+ *                              variance (layernorm.py:40-42, :138-140)
+ *   x, add, x_out, y  [rows, cols] bf16
+ *   gate, scale, shift [rows / batch_rows, cols] fp32 (row r uses entry r / batch_rows)
+ *   weight, bias      [cols] fp32 (NULL: omitted)
+ * scale and shift are given together or not at all.
+ */
+typedef enum pasa_dit_norm {
+  PASA_DIT_RMSNORM = 0,
+  PASA_DIT_LAYERNORM = 1,
+  PASA_DIT_LAYERNORM_PADDED = 2
+} pasa_dit_norm;
+
+PASA_API int pasa_dit_row_norm(void* stream, const void* x, const void* add, const float* gate, void* x_out,
+              const float* weight, const float* bias, const float* scale, const float* shift,
+              int64_t rows, int64_t batch_rows, int cols, float eps, int norm, void* y);
+
+/*
+ * Self-attention producer: RMSNorm of the q and k rows over cols = heads *
+ * head_dim, the rotary embedding of every head's (2i, 2i+1) pairs as an fp64
+ * complex multiply, and the transpose to head-major.  Replaces get_qk_norm,
+ * get_transpose_qkv and apply_rotary_emb of the Wan processor
+ * (svg/models/wan/attention.py:122-149 and its torch rotary path :49-57):
+ *   xq, xk, xv  [batch, tokens, cols] bf16 (xk / xv may be NULL: skipped)
+ *   wq, wk      [cols] fp32 RMSNorm weights
+ *   cos, sin    [tokens, head_dim / 2] fp64, or both NULL (no rotation)
+ *   q, k, v     head_major ? [batch, heads, tokens, head_dim] : [batch, tokens, cols]
+ * q = bf16(rotate(bf16(xq * rstd * wq))), rotate in fp64 and rounded to bf16
+ * through fp32; v is copied.  Outputs must not overlap the inputs.
+ */
+PASA_API int pasa_dit_qkv_rope(void* stream, const void* xq, const void* xk, const void* xv,
+              const float* wq, const float* wk, const double* cos, const double* sin,
+              int64_t batch, int64_t tokens, int heads, int head_dim, float eps, int head_major,
+              void* q, void* k, void* v);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,12 @@ cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const vo
                            const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*, int);
 cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
                          int64_t, int64_t, int64_t, int);
+int dit_max_cols();
+cudaError_t launch_row_norm(cudaStream_t, const void*, const void*, const float*, void*, const float*, const float*,
+                            const float*, const float*, int64_t, int64_t, int, float, int, int, void*);
+cudaError_t launch_qkv_rope(cudaStream_t, const void*, const void*, const void*, const float*, const float*,
+                            const double*, const double*, int64_t, int64_t, int, int, float, int, void*, void*,
+                            void*);
 }  // namespace pasa
 
 using namespace pasa;
@@ -58,6 +64,13 @@ int64_t top_k_of(double density, int64_t NT) {
   if (t < 1) t = 1;
   if (t > NT) t = NT;
   return t;
+}
+
+// cols rounded up to a power of two (the reference's Triton row programs)
+int padded_cols(int cols) {
+  int p = 1;
+  while (p < cols) p <<= 1;
+  return p;
 }
 
 int check_select_fit(int D, int64_t NT, int64_t NS) {
@@ -228,6 +241,46 @@ int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_
   if (st) return st;
   return cuda_status(launch_place(static_cast<cudaStream_t>(stream), src, dst, head_is_temporal, cfg, H, T, D,
                                   esize_of(dtype), context_length, num_frame, frame_size, inverse));
+}
+
+int pasa_dit_row_norm(void* stream, const void* x, const void* add, const float* gate, void* x_out,
+                      const float* weight, const float* bias, const float* scale, const float* shift, int64_t rows,
+                      int64_t batch_rows, int cols, float eps, int norm, void* y) {
+  if (norm != PASA_DIT_RMSNORM && norm != PASA_DIT_LAYERNORM && norm != PASA_DIT_LAYERNORM_PADDED)
+    return PASA_ERR_UNSUPPORTED;
+  if (rows < 1 || rows > INT32_MAX || cols < 8 || cols % 8 != 0 || cols > dit_max_cols()) return PASA_ERR_SHAPE;
+  if (batch_rows < 1 || rows % batch_rows != 0) return PASA_ERR_SHAPE;
+  if (!std::isfinite(eps) || eps < 0.f) return PASA_ERR_SHAPE;
+  if (!x || !y || (scale == nullptr) != (shift == nullptr)) return PASA_ERR_NULL;
+  if (gate && !add) return PASA_ERR_NULL;
+  const void* ptrs[] = {x, add, gate, x_out, weight, bias, scale, shift, y};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return PASA_ERR_ALIGN;
+  int st = check_device();
+  if (st) return st;
+  return cuda_status(launch_row_norm(static_cast<cudaStream_t>(stream), x, add, gate, add ? x_out : nullptr, weight,
+                                     bias, scale, shift, rows, batch_rows, cols, eps, norm != PASA_DIT_RMSNORM,
+                                     norm == PASA_DIT_LAYERNORM_PADDED ? padded_cols(cols) - cols : 0, y));
+}
+
+int pasa_dit_qkv_rope(void* stream, const void* xq, const void* xk, const void* xv, const float* wq, const float* wk,
+                      const double* cos, const double* sin, int64_t batch, int64_t tokens, int heads, int head_dim,
+                      float eps, int head_major, void* q, void* k, void* v) {
+  if (batch < 1 || tokens < 1 || heads < 1 || head_dim < 8 || head_dim % 8 != 0) return PASA_ERR_SHAPE;
+  const int64_t cols = int64_t(heads) * head_dim;
+  if (cols > dit_max_cols() || batch * tokens > INT32_MAX) return PASA_ERR_SHAPE;
+  if (!std::isfinite(eps) || eps < 0.f) return PASA_ERR_SHAPE;
+  if (!xq || !wq || !q || (cos == nullptr) != (sin == nullptr)) return PASA_ERR_NULL;
+  if (xk && (!wk || !k)) return PASA_ERR_NULL;
+  if (xv && !v) return PASA_ERR_NULL;
+  const void* ptrs[] = {xq, xk, xv, wq, wk, cos, sin, q, k, v};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return PASA_ERR_ALIGN;
+  int st = check_device();
+  if (st) return st;
+  return cuda_status(launch_qkv_rope(static_cast<cudaStream_t>(stream), xq, xk, xv, wq, wk, cos, sin, batch, tokens,
+                                     int(cols), head_dim, eps, head_major ? 1 : 0, q, xk ? k : nullptr,
+                                     xv ? v : nullptr));
 }
 
 }  // extern "C"

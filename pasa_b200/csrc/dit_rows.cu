@@ -1,0 +1,350 @@
+// Row kernels of the Wan2.1 DiT block around the attention op: the
+// elementwise work between the GEMMs, fused so that each activation row
+// crosses HBM once per use.  All are HBM-bound; one 128-thread CTA owns one
+// token row (cols <= 8192 bf16 = 16 KB), every thread a strided set of
+// 16-byte vectors kept in registers between the two reduction passes.
+//
+// row_norm_kernel — optional gated residual, then LayerNorm (centered) or
+// RMSNorm, optional affine, optional (1 + scale) / shift modulation:
+//     x'  = bf16(x + add * gate)          (custom_models.py:58-65, :82-83,
+//                                          modulate.py:90-122)
+//     y   = bf16(((x' - mean) * rstd) [* w + b] [* (1 + scale) + shift])
+//                                         (layernorm.py:13-58, :113-155,
+//                                          modulate.py:12-42, rmsnorm.py:8-48)
+//     mean = sum(x') / C,  var = sum((x' - mean)^2) / C,  rstd = 1 / sqrt(var + eps)
+// (optionally with the reference Triton LayerNorm's padding term: its rows are
+// padded with zeros to the next power of two and every padding column adds
+// (0 - mean)^2 to the sum of squares, layernorm.py:40-42)
+// The reference runs these as separate Triton kernels with fp32
+// intermediates in HBM; here the fp32 intermediates stay in registers, so the
+// values are the same while the traffic drops to one read and one write.
+//
+// qkv_rope_kernel — the self-attention producer: RMSNorm of the q and k rows
+// over the hidden dimension (rmsnorm.py:8-48, rounded to bf16), the rotary
+// embedding of each head's (2i, 2i+1) pairs as a complex multiply in fp64
+// (the reference's fallback, svg/models/wan/attention.py:49-57: bf16 ->
+// float64, times cos + i sin, -> bf16 through float32 as torch casts), and the
+// [B, T, H*D] -> [B, H, T, D] transpose of q, k and v (attention.py:136-141),
+// all in one pass.
+//
+// Arithmetic is written with explicit round-to-nearest intrinsics (no fused
+// multiply-add) and a fixed reduction order: per thread in vector order, then
+// an xor butterfly over the warp, then the four warp sums in order.  The CPU
+// restatement in the test oracle follows the same order, so the results
+// compare bit for bit.
+#include "common.cuh"
+
+namespace pasa {
+namespace {
+
+constexpr int kRowThreads = 128;
+constexpr int kRowWarps = kRowThreads / 32;
+constexpr int kMaxVec = 8;  // 16-byte vectors per thread: cols <= 8 * 8 * 128
+// Kernels are instantiated for V = ceil(cols / (8 * 128)) vectors per thread,
+// so the register arrays are no larger than the row needs (V = 5 at C = 5120).
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* out) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* in) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void load8f(const float* p, float* out) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
+__device__ __forceinline__ float bf16_rn(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Sum over the CTA in a fixed order; every thread gets the same value.
+__device__ __forceinline__ float block_sum(float acc, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int w = 1; w < kRowWarps; ++w) t = __fadd_rn(t, red[w]);
+  __syncthreads();  // red is reused by the next reduction
+  return t;
+}
+
+struct RowNormArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* add;  // residual branch, or null
+  const float* gate;         // [B, C] gate of the residual branch, or null (plain add)
+  __nv_bfloat16* x_out;      // updated residual stream (may alias x), or null
+  const float* w;            // [C] affine weight, or null
+  const float* b;            // [C] affine bias, or null
+  const float* scale;        // [B, C] modulation, or null (then shift is ignored)
+  const float* shift;        // [B, C]
+  __nv_bfloat16* y;
+  int64_t batch_rows;        // rows per batch entry of gate / scale / shift
+  int cols;
+  float eps;
+  int center;                // 1: LayerNorm, 0: RMSNorm
+  int pad_cols;              // > 0: add pad_cols * mean^2 to the sum of squares
+};
+
+template <int V>
+__global__ void __launch_bounds__(kRowThreads) row_norm_kernel(RowNormArgs a) {
+  __shared__ float red[kRowWarps];
+  const int64_t row = blockIdx.x;
+  const int nvec = a.cols >> 3;
+  const int tid = threadIdx.x;
+  const int64_t base = row * a.cols;
+  const int64_t vb = (row / a.batch_rows) * a.cols;
+
+  float v[V][8];
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = tid + i * kRowThreads;
+    if (j < nvec) {
+      load8(a.x + base + 8 * j, v[i]);
+      if (a.add != nullptr) {
+        float r[8];
+        load8(a.add + base + 8 * j, r);
+        if (a.gate != nullptr) {
+          float g[8];
+          load8f(a.gate + vb + 8 * j, g);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) r[e] = __fmul_rn(r[e], g[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = bf16_rn(__fadd_rn(v[i][e], r[e]));
+        if (a.x_out != nullptr) store8(a.x_out + base + 8 * j, v[i]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, v[i][e]);
+    }
+  }
+  const float mean = a.center ? __fdiv_rn(block_sum(acc, red), float(a.cols)) : 0.f;
+  float acc2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    if (tid + i * kRowThreads < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = __fsub_rn(v[i][e], mean);
+        acc2 = __fadd_rn(acc2, __fmul_rn(d, d));
+      }
+    }
+  }
+  float ssq = block_sum(acc2, red);
+  if (a.pad_cols > 0) ssq = __fadd_rn(ssq, __fmul_rn(float(a.pad_cols), __fmul_rn(mean, mean)));
+  const float var = __fdiv_rn(ssq, float(a.cols));
+  const float rstd = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = tid + i * kRowThreads;
+    if (j < nvec) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(__fsub_rn(v[i][e], mean), rstd);
+      if (a.w != nullptr) {
+        float w[8];
+        load8f(a.w + 8 * j, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(o[e], w[e]);
+      }
+      if (a.b != nullptr) {
+        float b[8];
+        load8f(a.b + 8 * j, b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(o[e], b[e]);
+      }
+      if (a.scale != nullptr) {
+        float s[8], h[8];
+        load8f(a.scale + vb + 8 * j, s);
+        load8f(a.shift + vb + 8 * j, h);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(__fmul_rn(o[e], __fadd_rn(1.f, s[e])), h[e]);
+      }
+      store8(a.y + base + 8 * j, o);
+    }
+  }
+}
+
+struct QkvArgs {
+  const __nv_bfloat16* xq;
+  const __nv_bfloat16* xk;  // or null
+  const __nv_bfloat16* xv;  // or null
+  const float* wq;
+  const float* wk;
+  const double* cos;        // [tokens, D/2] or null (no rotation)
+  const double* sin;
+  __nv_bfloat16* q;
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  int64_t tokens;
+  int cols, head_dim;
+  float eps;
+  int head_major;           // 1: [B, H, tokens, D]; 0: [B, tokens, H*D]
+};
+
+__device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t bidx, int64_t t, int c) {
+  if (!a.head_major) return (bidx * a.tokens + t) * a.cols + c;
+  const int h = c / a.head_dim, d = c - h * a.head_dim;
+  const int64_t H = a.cols / a.head_dim;
+  return ((bidx * H + h) * a.tokens + t) * a.head_dim + d;
+}
+
+// RMSNorm of one row (bf16 out), then the rotation of its pairs.
+template <int V>
+__device__ __forceinline__ void norm_rope_row(const QkvArgs& a, const __nv_bfloat16* x, const float* w,
+                                              __nv_bfloat16* out, int64_t bidx, int64_t t, float* red) {
+  const int nvec = a.cols >> 3;
+  const int tid = threadIdx.x;
+  const __nv_bfloat16* xr = x + (bidx * a.tokens + t) * a.cols;
+  float v[V][8];
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = tid + i * kRowThreads;
+    if (j < nvec) {
+      load8(xr + 8 * j, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, __fmul_rn(v[i][e], v[i][e]));
+    }
+  }
+  const float var = __fdiv_rn(block_sum(acc, red), float(a.cols));
+  const float rstd = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+  const int half = a.head_dim >> 1;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = tid + i * kRowThreads;
+    if (j < nvec) {
+      const int c = 8 * j;
+      float wv[8], o[8];
+      load8f(w + c, wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = bf16_rn(__fmul_rn(__fmul_rn(v[i][e], rstd), wv[e]));
+      if (a.cos != nullptr) {
+        const int p0 = (c % a.head_dim) >> 1;
+        const double* cp = a.cos + t * half + p0;
+        const double* sp = a.sin + t * half + p0;
+        const double2 c01 = *reinterpret_cast<const double2*>(cp);
+        const double2 c23 = *reinterpret_cast<const double2*>(cp + 2);
+        const double2 s01 = *reinterpret_cast<const double2*>(sp);
+        const double2 s23 = *reinterpret_cast<const double2*>(sp + 2);
+        const double cs[4] = {c01.x, c01.y, c23.x, c23.y};
+        const double sn[4] = {s01.x, s01.y, s23.x, s23.y};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const double re = o[2 * p], im = o[2 * p + 1];
+          o[2 * p] = __double2float_rn(__dsub_rn(__dmul_rn(re, cs[p]), __dmul_rn(im, sn[p])));
+          o[2 * p + 1] = __double2float_rn(__dadd_rn(__dmul_rn(re, sn[p]), __dmul_rn(im, cs[p])));
+        }
+      }
+      store8(out + out_offset(a, bidx, t, c), o);
+    }
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(kRowThreads) qkv_rope_kernel(QkvArgs a) {
+  __shared__ float red[kRowWarps];
+  const int64_t row = blockIdx.x;
+  const int64_t bidx = row / a.tokens, t = row - bidx * a.tokens;
+  norm_rope_row<V>(a, a.xq, a.wq, a.q, bidx, t, red);
+  if (a.xk != nullptr) norm_rope_row<V>(a, a.xk, a.wk, a.k, bidx, t, red);
+  if (a.xv != nullptr) {
+    const int nvec = a.cols >> 3;
+    const __nv_bfloat16* xr = a.xv + row * a.cols;
+    for (int j = threadIdx.x; j < nvec; j += kRowThreads) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + 8 * j);
+      *reinterpret_cast<uint4*>(a.v + out_offset(a, bidx, t, 8 * j)) = u;
+    }
+  }
+}
+
+int vectors_per_thread(int cols) { return int(cdiv(cols / 8, kRowThreads)); }
+
+}  // namespace
+
+int dit_row_threads() { return kRowThreads; }
+int dit_max_cols() { return kMaxVec * 8 * kRowThreads; }
+
+cudaError_t launch_row_norm(cudaStream_t stream, const void* x, const void* add, const float* gate, void* x_out,
+                            const float* w, const float* b, const float* scale, const float* shift, int64_t rows,
+                            int64_t batch_rows, int cols, float eps, int center, int pad_cols, void* y) {
+  RowNormArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.add = static_cast<const __nv_bfloat16*>(add);
+  a.gate = gate;
+  a.x_out = static_cast<__nv_bfloat16*>(x_out);
+  a.w = w;
+  a.b = b;
+  a.scale = scale;
+  a.shift = shift;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.batch_rows = batch_rows;
+  a.cols = cols;
+  a.eps = eps;
+  a.center = center;
+  a.pad_cols = pad_cols;
+  const dim3 grid{unsigned(rows)};
+  switch (vectors_per_thread(cols)) {
+    case 1: row_norm_kernel<1><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 2: row_norm_kernel<2><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 3: row_norm_kernel<3><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 4: row_norm_kernel<4><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 5: row_norm_kernel<5><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 6: row_norm_kernel<6><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 7: row_norm_kernel<7><<<grid, kRowThreads, 0, stream>>>(a); break;
+    default: row_norm_kernel<8><<<grid, kRowThreads, 0, stream>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qkv_rope(cudaStream_t stream, const void* xq, const void* xk, const void* xv, const float* wq,
+                            const float* wk, const double* cos, const double* sin, int64_t batch, int64_t tokens,
+                            int cols, int head_dim, float eps, int head_major, void* q, void* k, void* v) {
+  QkvArgs a;
+  a.xq = static_cast<const __nv_bfloat16*>(xq);
+  a.xk = static_cast<const __nv_bfloat16*>(xk);
+  a.xv = static_cast<const __nv_bfloat16*>(xv);
+  a.wq = wq;
+  a.wk = wk;
+  a.cos = cos;
+  a.sin = sin;
+  a.q = static_cast<__nv_bfloat16*>(q);
+  a.k = static_cast<__nv_bfloat16*>(k);
+  a.v = static_cast<__nv_bfloat16*>(v);
+  a.tokens = tokens;
+  a.cols = cols;
+  a.head_dim = head_dim;
+  a.eps = eps;
+  a.head_major = head_major;
+  const dim3 grid{unsigned(batch * tokens)};
+  switch (vectors_per_thread(cols)) {
+    case 1: qkv_rope_kernel<1><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 2: qkv_rope_kernel<2><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 3: qkv_rope_kernel<3><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 4: qkv_rope_kernel<4><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 5: qkv_rope_kernel<5><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 6: qkv_rope_kernel<6><<<grid, kRowThreads, 0, stream>>>(a); break;
+    case 7: qkv_rope_kernel<7><<<grid, kRowThreads, 0, stream>>>(a); break;
+    default: qkv_rope_kernel<8><<<grid, kRowThreads, 0, stream>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pasa

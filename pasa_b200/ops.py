@@ -268,6 +268,95 @@ def dense_attention(q, k, v, scale=None):
     return o
 
 
+# ---------------------------------------------------------------------------
+# DiT row kernels around the attention op (pasa_dit_row_norm, pasa_dit_qkv_rope)
+# ---------------------------------------------------------------------------
+def _vec(t: Optional[torch.Tensor], cols: int, name: str) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    if t.dtype != torch.float32 or not t.is_cuda or t.shape[-1] != cols:
+        raise ValueError(f"{name} must be an fp32 CUDA tensor with last dimension {cols}")
+    return t.contiguous()
+
+
+DIT_RMSNORM, DIT_LAYERNORM, DIT_LAYERNORM_PADDED = 0, 1, 2
+
+
+def dit_row_norm(x, *, add=None, gate=None, x_out=None, weight=None, bias=None, scale=None, shift=None,
+                 eps: float = 1e-6, norm: int = DIT_LAYERNORM, out=None):
+    """Gated residual + LayerNorm / RMSNorm + affine + modulation over the last
+    dimension of bf16 ``x`` [B, L, C] in one pass (pasa_dit_row_norm):
+
+        x' = x + add * gate  (or x + add; x when add is None), written to x_out
+        y  = ((x' - mean) * rstd) [* weight] [+ bias] [* (1 + scale) + shift]
+
+    ``norm``: DIT_LAYERNORM (the torch LayerNorm), DIT_RMSNORM (mean 0), or
+    DIT_LAYERNORM_PADDED (the reference's Triton LayerNorm, whose zero padding
+    to a power of two adds (P - C) * mean^2 to the variance).
+
+    ``gate``, ``scale``, ``shift`` are fp32 [B, 1, C] or [C] (one vector per
+    batch entry), ``weight`` and ``bias`` fp32 [C].  Returns y (bf16, like x).
+    """
+    if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous bf16 CUDA tensor")
+    C = x.shape[-1]
+    rows = x.numel() // C
+    batch = x.shape[0] if x.dim() == 3 else 1
+    for t, n in ((add, "add"), (x_out, "x_out")):
+        if t is not None and (t.shape != x.shape or t.dtype != x.dtype or not t.is_contiguous()):
+            raise ValueError(f"{n} must be a contiguous bf16 tensor shaped like x")
+    per_batch = []
+    for t, n in ((gate, "gate"), (scale, "scale"), (shift, "shift")):
+        t = _vec(t, C, n)
+        if t is not None and t.numel() not in (C, batch * C):
+            raise ValueError(f"{n} must hold one [C] vector per batch entry")
+        if t is not None and t.numel() == C and batch > 1:
+            t = t.reshape(1, C).expand(batch, C).contiguous()
+        per_batch.append(t)
+    gate, scale, shift = per_batch
+    weight, bias = _vec(weight, C, "weight"), _vec(bias, C, "bias")
+    y = torch.empty_like(x) if out is None else out
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        _lib.check("pasa_dit_row_norm", lib.pasa_dit_row_norm(
+            _stream_ptr(x.device), x.data_ptr(), _ptr(add), _ptr(gate), _ptr(x_out), _ptr(weight), _ptr(bias),
+            _ptr(scale), _ptr(shift), rows, rows // batch, C, float(eps), int(norm), y.data_ptr()))
+    return y
+
+
+def dit_qkv_rope(xq, xk, xv, wq, wk, cos, sin, heads: int, eps: float = 1e-6, head_major: bool = True):
+    """Self-attention producer (pasa_dit_qkv_rope): RMSNorm of the bf16 q and k
+    projections [B, L, H*D] with fp32 weights [H*D], fp64 rotary embedding
+    (``cos``, ``sin`` [L, D/2] float64, or None) and the transpose to
+    [B, H, L, D] (``head_major``); v is transposed.  ``xk`` / ``xv`` may be
+    None.  Returns (q, k, v) with None for the skipped ones."""
+    for t, n in ((xq, "xq"), (xk, "xk"), (xv, "xv")):
+        if t is not None and (t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous() or t.dim() != 3
+                              or t.shape != xq.shape):
+            raise ValueError(f"{n} must be a contiguous bf16 CUDA tensor [B, L, C] like xq")
+    B, L, C = xq.shape
+    if C % heads:
+        raise ValueError("hidden size is not a multiple of heads")
+    D = C // heads
+    wq, wk = _vec(wq, C, "wq"), _vec(wk, C, "wk")
+    if (cos is None) != (sin is None):
+        raise ValueError("cos and sin are given together")
+    if cos is not None:
+        if cos.dtype != torch.float64 or sin.dtype != torch.float64 or cos.shape != (L, D // 2) \
+                or sin.shape != (L, D // 2):
+            raise ValueError(f"cos, sin must be float64 [{L}, {D // 2}]")
+        cos, sin = cos.contiguous(), sin.contiguous()
+    shape = (B, heads, L, D) if head_major else (B, L, C)
+    outs = [torch.empty(shape, dtype=torch.bfloat16, device=xq.device) if t is not None else None
+            for t in (xq, xk, xv)]
+    lib = _lib.load()
+    with torch.cuda.device(xq.device):
+        _lib.check("pasa_dit_qkv_rope", lib.pasa_dit_qkv_rope(
+            _stream_ptr(xq.device), xq.data_ptr(), _ptr(xk), _ptr(xv), wq.data_ptr(), _ptr(wk), _ptr(cos),
+            _ptr(sin), B, L, heads, D, float(eps), int(bool(head_major)), *(_ptr(t) for t in outs)))
+    return tuple(outs)
+
+
 def piecewise_sparse_attention(q, k, v, density=0.15, block_size=64, use_random=False, **kwargs):
     """The name the model processors call (svg/models/wan/attention.py:384,
     svg/models/hyvideo/attention.py:640, :682); its source is not in the

@@ -83,3 +83,21 @@ def test_entry_points_validate_before_touching_the_device():
                             0) == _lib.ERR_WORKSPACE
     # placement: seq_len must be context + frames * frame_size (placement.py:128)
     assert lib.pasa_place(None, p, p, p, 1, 2, 100, 64, _lib.BF16, 4, 3, 30, 0) == _lib.ERR_SHAPE
+    # DiT row kernels: cols a multiple of 8 and at most 8192, known norm mode,
+    # gate only with add, scale and shift together, 16-byte alignment
+    rn = lambda x, add, gate, scale, shift, rows, brows, cols, norm: lib.pasa_dit_row_norm(
+        None, x, add, gate, None, None, None, scale, shift, rows, brows, cols, 1e-6, norm, p)
+    assert rn(p, None, None, None, None, 4, 4, 5121, 1) == _lib.ERR_SHAPE
+    assert rn(p, None, None, None, None, 4, 4, 8200, 1) == _lib.ERR_SHAPE
+    assert rn(p, None, None, None, None, 4, 3, 64, 1) == _lib.ERR_SHAPE       # rows % batch_rows
+    assert rn(p, None, None, None, None, 4, 4, 64, 3) == _lib.ERR_UNSUPPORTED
+    assert rn(p, None, p, None, None, 4, 4, 64, 1) == _lib.ERR_NULL           # gate without add
+    assert rn(p, None, None, p, None, 4, 4, 64, 1) == _lib.ERR_NULL           # scale without shift
+    assert rn(bad, None, None, None, None, 4, 4, 64, 1) == _lib.ERR_ALIGN
+    qr = lambda xq, xk, wk, cos, sin, heads, hd: lib.pasa_dit_qkv_rope(
+        None, xq, xk, None, p, wk, cos, sin, 1, 16, heads, hd, 1e-6, 1, p, p, None)
+    assert qr(p, None, None, None, None, 40, 12) == _lib.ERR_SHAPE            # head_dim % 8
+    assert qr(p, None, None, None, None, 80, 128) == _lib.ERR_SHAPE           # cols > 8192
+    assert qr(p, p, None, None, None, 40, 128) == _lib.ERR_NULL               # xk without wk
+    assert qr(p, None, None, p, None, 40, 128) == _lib.ERR_NULL               # cos without sin
+    assert qr(bad, None, None, None, None, 40, 128) == _lib.ERR_ALIGN
