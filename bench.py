@@ -59,6 +59,7 @@ def parse():
                     help="time the full Wan2.1-14B DiT denoising step (PASA in every layer, Ulysses over ranks)")
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks in the DiT step (40 = the full model)")
     ap.add_argument("--dit-density", type=float, default=0.1)
+    ap.add_argument("--dit-frames", type=int, default=0, help="latent frames (0 = 21, the 81-frame video)")
     ap.add_argument("--dit-torch", action="store_true",
                     help="DiT step with torch elementwise ops instead of the row kernels (comparison)")
     return ap.parse_args()
@@ -240,6 +241,8 @@ def run_dit(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg = dataclasses.replace(dit.WAN14B_720P, layers=args.dit_layers, density=args.dit_density)
+    if args.dit_frames:
+        cfg = dataclasses.replace(cfg, frames=args.dit_frames)
     if cfg.heads % world:
         raise SystemExit(f"{cfg.heads} heads do not split over {world} ranks")
     group = dist.group.WORLD if world > 1 else None
@@ -259,12 +262,25 @@ def run_dit(args):
     timestep = torch.tensor([900], device=dev)
     lat_d, text_d = lat_h.to(dev), text_h.to(dev)
 
-    attn_events = []
+    attn_events, a2a_events = [], []
+
+    def timed(fn):
+        def run(t, g):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            r = fn(t, g)
+            e1.record(stream)
+            a2a_events.append((e0, e1))
+            return r
+        return run
+
+    # time the Ulysses all-to-alls (resharding copies included)
+    dit.seq_to_head, dit.head_to_tokens = timed(dit.seq_to_head), timed(dit.head_to_tokens)
 
     def core(q, k, v):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        o = ops.pisa_pg_attention(q, k, v, density=cfg.density)
+        o = ops.pisa_pg_attention(q, k, v, density=cfg.density, out_layout="bthd")
         e1.record(stream)
         attn_events.append((e0, e1))
         return o
@@ -286,6 +302,7 @@ def run_dit(args):
             step()
         torch.cuda.synchronize()
         attn_events.clear()
+        a2a_events.clear()
         gpu_ids = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip().isdigit()]
         sampler = ClockSampler([gpu_ids[local] if local < len(gpu_ids) else local])
         with sampler:
@@ -302,20 +319,22 @@ def run_dit(args):
         assert torch.isfinite(out).all()
         ms_step = max_over_ranks(start.elapsed_time(end) / args.steps, world)
         attn_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in attn_events) / args.steps, world)
+        a2a_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in a2a_events) / args.steps, world)
         attn_events.clear()
-
-        e2e_step()
-        torch.cuda.synchronize()
-        barrier(world)
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
-        for _ in range(args.steps):
+        e2e_ms = None
+        if not args.no_e2e:
             e2e_step()
-        s1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        e2e_ms = max_over_ranks(s0.elapsed_time(s1) / args.steps, world)
-        assert torch.isfinite(out_h.float()).all()
+            torch.cuda.synchronize()
+            barrier(world)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(args.steps):
+                e2e_step()
+            s1.record(stream)
+            torch.cuda.synchronize()
+            barrier(world)
+            e2e_ms = max_over_ranks(s0.elapsed_time(s1) / args.steps, world)
+            assert torch.isfinite(out_h.float()).all()
 
     clocks = sampler.summary()
     nbytes = lambda t: t.numel() * t.element_size()
@@ -332,17 +351,19 @@ def run_dit(args):
             "value": ms_step, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents and text embeddings, random-init weights)",
-            "config": {"workload": "wan14b-720p-dit-step", "layers": cfg.layers, "hidden": C, "heads": cfg.heads,
+            "config": {"workload": "wan14b-720p-dit-step" + (f"-{cfg.frames}f" if args.dit_frames else ""),
+                       "layers": cfg.layers, "hidden": C, "heads": cfg.heads,
                        "ffn": Fd, "tokens": tokens, "text_len": Lt, "density": cfg.density,
                        "parallelism": f"ulysses{world}" if world > 1 else "none",
                        "elementwise": "row kernels (pasa_dit_row_norm, pasa_dit_qkv_rope)" if fused else "torch ops",
                        "l2": "activations 0.77 GB per tensor > 126 MB L2; no flush"},
-            "kernels_ms": {"pasa_attention_per_step": attn_ms,
-                           "attention_share": attn_ms / ms_step},
+            "kernels_ms": {"pasa_attention_per_step": attn_ms, "attention_share": attn_ms / ms_step,
+                           "ulysses_all_to_all_per_step": a2a_ms if world > 1 else 0.0},
             "gemm_tflop_per_step": gemm / 1e12,
-            "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": (nbytes(lat_h) + nbytes(text_h)) * world,
-                    "d2h_bytes_per_step": nbytes(out_h) * world,
-                    "note": "dit.step from pinned host latents/text to pinned host output, per rank, summed over ranks"},
+            "e2e": None if e2e_ms is None else {
+                "value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": (nbytes(lat_h) + nbytes(text_h)) * world,
+                "d2h_bytes_per_step": nbytes(out_h) * world,
+                "note": "dit.step from pinned host latents/text to pinned host output, per rank, summed over ranks"},
             "clocks": clocks,
             # per block: prep, select, attention, plus with the row kernels 3 norms
             # and 3 producers (q/k/v, cross q, cross k); one more norm per step

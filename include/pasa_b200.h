@@ -151,6 +151,23 @@ PASA_API int pasa_forward(void* stream, const void* q, const void* k, const void
                  double density, float scale, int use_cov_bias, const float* noise,
                  void* workspace, size_t workspace_bytes, void* o, int kernel);
 
+/* Output layouts of pasa_forward_ex. */
+typedef enum pasa_o_layout {
+  PASA_O_BHTD = 0,  /* o [B*H, T, D] (head-major), as pasa_forward           */
+  PASA_O_BTHD = 1   /* o [B, T, H, D] (token-major): the layout the output
+                       projection after the attention reads, so the
+                       transpose the reference's processors run after it
+                       (attention.py:154, get_o) is not a copy; tcgen05
+                       kernel only                                          */
+} pasa_o_layout;
+
+/* pasa_forward with the output layout chosen by o_layout (same arguments
+ * otherwise; pasa_forward is o_layout = PASA_O_BHTD). */
+PASA_API int pasa_forward_ex(void* stream, const void* q, const void* k, const void* v,
+                int64_t B, int64_t H, int64_t T, int D, int dtype, double density, float scale,
+                int use_cov_bias, const float* noise, void* workspace, size_t workspace_bytes,
+                void* o, int kernel, int o_layout);
+
 /*
  * The whole op like pasa_forward, but with no workspace argument and no
  * allocation anywhere: the scratch (block statistics, top-k indices,

@@ -33,11 +33,14 @@ ATTN_SIMT = 2
 
 DEVERR_WAIT_TIMEOUT = 0x1
 
+O_BHTD = 0
+O_BTHD = 1
+
 EXPORTS = (
     "pasa_abi_version", "pasa_status_string", "pasa_derive", "pasa_workspace_size", "pasa_prep",
     "pasa_select", "pasa_attn", "pasa_forward", "pasa_forward_noalloc", "pasa_place",
     "pasa_forward_host_workspace_size", "pasa_forward_host", "pasa_dense_attn",
-    "pasa_dit_row_norm", "pasa_dit_qkv_rope",
+    "pasa_dit_row_norm", "pasa_dit_qkv_rope", "pasa_forward_ex",
 )
 
 _lib = None
@@ -75,6 +78,8 @@ def load() -> ctypes.CDLL:
         "pasa_forward_host": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float, c_int,
                                       P, P, c_size_t, c_int64, P, POINTER(c_uint32), c_int]),
         "pasa_dense_attn": (c_int, [P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, P, P]),
+        "pasa_forward_ex": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float,
+                                    c_int, P, P, c_size_t, P, c_int, c_int]),
         "pasa_dit_row_norm": (c_int, [P, P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_float, c_int, P]),
         "pasa_dit_qkv_rope": (c_int, [P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, c_int,
                                       P, P, P]),

@@ -113,6 +113,7 @@ struct Params {
   const uint32_t* sel_mask;
   uint32_t* err;
   int dense;  // every key block selected for every query block (sel_mask unused, no phase 2)
+  int64_t o_heads;  // 0: o is [B*H, T, D]; H > 0: o is [B, T, H, D] (token-major, bh = b*H + h)
 };
 
 // Optional step tracer (compile with -DPASA_TRACE): one CTA, chosen with
@@ -689,7 +690,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         const bool store = t < P.T;
         const float denom = l_tot + g_tot * fast_exp2(m_true - m_used);
         const float inv = 1.0f / denom;
-        __nv_bfloat16* orow = P.o + (bh * P.T + t) * D + set * DH;
+        const int64_t orow_idx = P.o_heads > 0
+                                     ? ((bh / P.o_heads) * P.T + t) * P.o_heads + bh % P.o_heads
+                                     : bh * P.T + t;
+        __nv_bfloat16* orow = P.o + orow_idx * D + set * DH;
 #pragma unroll
         for (int c0 = 0; c0 < DH; c0 += 16) {
           uint32_t v[16];
@@ -750,7 +754,7 @@ bool make_map(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t bat
 template <int D>
 cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const void* v, const void* kc,
                         const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
-                        float scale, void* o, uint32_t* err, int dense) {
+                        float scale, void* o, uint32_t* err, int dense, int64_t o_heads) {
   using C = Cfg<D>;
   const int64_t NT = cdiv(T_len, kBlock), NG = cdiv(NT, kGroup), NTP = NG * kGroup;
   if (NT > kMaxNT) return cudaErrorInvalidValue;
@@ -762,6 +766,7 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
   Params p;
   p.T = T_len; p.NT = NT; p.NG = NG; p.NTP = NTP; p.scale = scale;
   p.o = static_cast<__nv_bfloat16*>(o); p.sel_mask = mask; p.err = err; p.dense = dense;
+  p.o_heads = o_heads;
   auto kern = attn_tc_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -774,9 +779,9 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
 
 cudaError_t launch_attn_tc(cudaStream_t st, int D, const void* q, const void* k, const void* v, const void* kc,
                            const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
-                           int64_t /*NS*/, float scale, void* o, uint32_t* err, int dense) {
-  if (D == 64) return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense);
-  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense);
+                           int64_t /*NS*/, float scale, void* o, uint32_t* err, int dense, int64_t o_heads) {
+  if (D == 64) return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads);
+  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads);
 }
 
 }  // namespace pasa

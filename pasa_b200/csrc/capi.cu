@@ -16,7 +16,8 @@ cudaError_t launch_attn_simt(cudaStream_t, int, int, const void*, const void*, c
                              const void*, const void*, const int32_t*, const uint32_t*, int64_t, int64_t,
                              int64_t, float, void*);
 cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const void*, const void*, const void*,
-                           const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*, int);
+                           const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*, int,
+                           int64_t);
 cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
                          int64_t, int64_t, int64_t, int);
 int dit_max_cols();
@@ -156,9 +157,14 @@ int pasa_select(void* stream, const void* qc, const void* kc, const float* h_nor
                                    sel_mask));
 }
 
-int pasa_attn(void* stream, const void* q, const void* k, const void* v, const void* kc, const void* vc,
-              const void* h_group, const int32_t* indices, const uint32_t* sel_mask, int64_t BH, int64_t T, int D,
-              int dtype, float scale, int64_t ns, void* o, uint32_t* err_word, int kernel) {
+namespace {
+
+// pasa_attn with the output layout: o_heads = 0 writes [B*H, T, D], o_heads =
+// H > 0 writes [B, T, H, D] (tensor-core kernel only).
+int attn_dispatch(void* stream, const void* q, const void* k, const void* v, const void* kc, const void* vc,
+                  const void* h_group, const int32_t* indices, const uint32_t* sel_mask, int64_t BH, int64_t T,
+                  int D, int dtype, float scale, int64_t ns, void* o, uint32_t* err_word, int kernel,
+                  int64_t o_heads) {
   int st = check_common(BH, T, D, dtype);
   if (st) return st;
   const int64_t NT = cdiv(T, kBlock), NG = cdiv(NT, kGroup);
@@ -169,23 +175,43 @@ int pasa_attn(void* stream, const void* q, const void* k, const void* v, const v
     return PASA_ERR_ALIGN;
   if (!std::isfinite(scale)) return PASA_ERR_SHAPE;
   if (kernel == PASA_ATTN_AUTO) kernel = (dtype == PASA_BF16) ? PASA_ATTN_TCGEN05 : PASA_ATTN_SIMT;
+  if (o_heads < 0 || (o_heads > 0 && BH % o_heads != 0)) return PASA_ERR_SHAPE;
   if ((st = check_device())) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (kernel == PASA_ATTN_TCGEN05) {
     if (dtype != PASA_BF16) return PASA_ERR_DTYPE;
-    return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word, 0));
+    return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word, 0,
+                                      o_heads));
   }
   if (kernel != PASA_ATTN_SIMT) return PASA_ERR_UNSUPPORTED;
+  if (o_heads > 0) return PASA_ERR_UNSUPPORTED;  // the CUDA-core kernel writes [B*H, T, D] only
   if (!indices) return PASA_ERR_NULL;
   if (NG > 64) return PASA_ERR_SHAPE;  // the CUDA-core kernel keeps one word per group in shared memory
   return cuda_status(launch_attn_simt(s, dtype, D, q, k, v, kc, vc, h_group, indices, sel_mask, BH, T, ns, scale,
                                       o));
 }
 
+}  // namespace
+
+int pasa_attn(void* stream, const void* q, const void* k, const void* v, const void* kc, const void* vc,
+              const void* h_group, const int32_t* indices, const uint32_t* sel_mask, int64_t BH, int64_t T, int D,
+              int dtype, float scale, int64_t ns, void* o, uint32_t* err_word, int kernel) {
+  return attn_dispatch(stream, q, k, v, kc, vc, h_group, indices, sel_mask, BH, T, D, dtype, scale, ns, o,
+                       err_word, kernel, 0);
+}
+
 int pasa_forward(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
                  int dtype, double density, float scale, int use_cov_bias, const float* noise, void* workspace,
                  size_t workspace_bytes, void* o, int kernel) {
+  return pasa_forward_ex(stream, q, k, v, B, H, T, D, dtype, density, scale, use_cov_bias, noise, workspace,
+                         workspace_bytes, o, kernel, PASA_O_BHTD);
+}
+
+int pasa_forward_ex(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T,
+                    int D, int dtype, double density, float scale, int use_cov_bias, const float* noise,
+                    void* workspace, size_t workspace_bytes, void* o, int kernel, int o_layout) {
   if (B < 1 || H < 1) return PASA_ERR_SHAPE;
+  if (o_layout != PASA_O_BHTD && o_layout != PASA_O_BTHD) return PASA_ERR_UNSUPPORTED;
   int st = check_common(B * H, T, D, dtype);
   if (st) return st;
   if (!std::isfinite(density)) return PASA_ERR_DENSITY;
@@ -211,7 +237,8 @@ int pasa_forward(void* stream, const void* q, const void* k, const void* v, int6
   if ((st = pasa_select(stream, qc, kc, hn, noise, BH, NT, D, dtype, scale, use_cov_bias, NS, idx, mask)))
     return st;
   if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
-  return pasa_attn(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel);
+  return attn_dispatch(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel,
+                       o_layout == PASA_O_BTHD ? H : 0);
 }
 
 int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, int64_t BH, int64_t T, int D,
@@ -225,7 +252,7 @@ int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, i
   if ((st = check_device())) return st;
   // the block statistics are not read in dense mode; q stands in for their (unused) tensor maps
   return cuda_status(launch_attn_tc(static_cast<cudaStream_t>(stream), D, q, k, v, q, q, q, nullptr, BH, T,
-                                    cdiv(T, kBlock), scale, o, err_word, 1));
+                                    cdiv(T, kBlock), scale, o, err_word, 1, 0));
 }
 
 int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal, int64_t cfg, int64_t H,

@@ -1,8 +1,6 @@
 // Row kernels of the Wan2.1 DiT block around the attention op: the
 // elementwise work between the GEMMs, fused so that each activation row
-// crosses HBM once per use.  All are HBM-bound; one 128-thread CTA owns one
-// token row (cols <= 8192 bf16 = 16 KB), every thread a strided set of
-// 16-byte vectors kept in registers between the two reduction passes.
+// crosses HBM once per use.  All are HBM-bound.
 //
 // row_norm_kernel — optional gated residual, then LayerNorm (centered) or
 // RMSNorm, optional affine, optional (1 + scale) / shift modulation:
@@ -27,11 +25,22 @@
 // [B, T, H*D] -> [B, H, T, D] transpose of q, k and v (attention.py:136-141),
 // all in one pass.
 //
+// Data movement (B200): one 128-thread CTA per token row; every thread
+// issues all of its 16-byte loads of the row (and of the residual branch /
+// the k and v rows) before using any, and holds the row between the two
+// reduction passes as packed bf16 (the values are bf16-exact), which keeps the
+// register footprint small enough for 12 CTAs per SM: rows of many CTAs are
+// in flight at once, which is what an HBM-bound row op needs.  Outputs are
+// written with 16-byte stores straight from registers.  (A variant that
+// staged rows through a shared-memory ring filled by bulk copies, with fewer
+// CTAs per SM, was slower: per row the work is a few thousand warp
+// instructions, so the kernel needs many resident rows, not deep prefetch.)
+//
 // Arithmetic is written with explicit round-to-nearest intrinsics (no fused
-// multiply-add) and a fixed reduction order: per thread in vector order, then
-// an xor butterfly over the warp, then the four warp sums in order.  The CPU
-// restatement in the test oracle follows the same order, so the results
-// compare bit for bit.
+// multiply-add) and a fixed reduction order: per thread in vector order
+// (thread t owns the 16-byte vectors t, t + 128, ...), then an xor butterfly
+// over the warp, then the four warp sums in order.  The CPU restatement in the
+// test oracle follows the same order, so the results compare bit for bit.
 #include "common.cuh"
 
 namespace pasa {
@@ -39,12 +48,13 @@ namespace {
 
 constexpr int kRowThreads = 128;
 constexpr int kRowWarps = kRowThreads / 32;
-constexpr int kMaxVec = 8;  // 16-byte vectors per thread: cols <= 8 * 8 * 128
+constexpr int kMaxVec = 8;        // 16-byte vectors per thread: cols <= 8 * 8 * 128
+constexpr int kRowMinBlocks = 8;  // resident CTAs per SM the register budget is cut for (row_norm)
+constexpr int kQkvMinBlocks = 6;  // the same for qkv_rope (two rows in registers)
 // Kernels are instantiated for V = ceil(cols / (8 * 128)) vectors per thread,
 // so the register arrays are no larger than the row needs (V = 5 at C = 5120).
 
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* out) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void unpack8(const uint4 u, float* out) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -53,24 +63,26 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* out) {
   }
 }
 
-__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* in) {
+// Round eight floats to bf16 (nearest even) and pack them.
+__device__ __forceinline__ uint4 pack8(const float* in) {
   uint32_t w[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
     w[i] = *reinterpret_cast<const uint32_t*>(&h);
   }
-  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+__device__ __forceinline__ uint4 ld16(const __nv_bfloat16* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ void st16(__nv_bfloat16* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+
 __device__ __forceinline__ void load8f(const float* p, float* out) {
-  const float4 a = *reinterpret_cast<const float4*>(p);
-  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
   out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
   out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
 }
-
-__device__ __forceinline__ float bf16_rn(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Sum over the CTA in a fixed order; every thread gets the same value.
 __device__ __forceinline__ float block_sum(float acc, float* red) {
@@ -82,6 +94,25 @@ __device__ __forceinline__ float block_sum(float acc, float* red) {
 #pragma unroll
   for (int w = 1; w < kRowWarps; ++w) t = __fadd_rn(t, red[w]);
   __syncthreads();  // red is reused by the next reduction
+  return t;
+}
+
+// Two independent sums with one pair of barriers (same order as block_sum).
+__device__ __forceinline__ float2 block_sum2(float a, float b, float2* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
+    b = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, off));
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(a, b);
+  __syncthreads();
+  float2 t = red[0];
+#pragma unroll
+  for (int w = 1; w < kRowWarps; ++w) {
+    t.x = __fadd_rn(t.x, red[w].x);
+    t.y = __fadd_rn(t.y, red[w].y);
+  }
+  __syncthreads();
   return t;
 }
 
@@ -103,24 +134,34 @@ struct RowNormArgs {
 };
 
 template <int V>
-__global__ void __launch_bounds__(kRowThreads) row_norm_kernel(RowNormArgs a) {
+__global__ void __launch_bounds__(kRowThreads, kRowMinBlocks) row_norm_kernel(RowNormArgs a) {
   __shared__ float red[kRowWarps];
   const int64_t row = blockIdx.x;
   const int nvec = a.cols >> 3;
   const int tid = threadIdx.x;
   const int64_t base = row * a.cols;
   const int64_t vb = (row / a.batch_rows) * a.cols;
+  const bool has_add = a.add != nullptr;
 
-  float v[V][8];
+  uint4 xv[V], av[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) {  // every load of the row in flight before any use
+    const int j = tid + k * kRowThreads;
+    if (j < nvec) {
+      xv[k] = ld16(a.x + base + 8 * j);
+      if (has_add) av[k] = ld16(a.add + base + 8 * j);
+    }
+  }
   float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int j = tid + i * kRowThreads;
+  for (int k = 0; k < V; ++k) {
+    const int j = tid + k * kRowThreads;
     if (j < nvec) {
-      load8(a.x + base + 8 * j, v[i]);
-      if (a.add != nullptr) {
+      float v[8];
+      unpack8(xv[k], v);
+      if (has_add) {
         float r[8];
-        load8(a.add + base + 8 * j, r);
+        unpack8(av[k], r);
         if (a.gate != nullptr) {
           float g[8];
           load8f(a.gate + vb + 8 * j, g);
@@ -128,36 +169,50 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(RowNormArgs a) {
           for (int e = 0; e < 8; ++e) r[e] = __fmul_rn(r[e], g[e]);
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = bf16_rn(__fadd_rn(v[i][e], r[e]));
-        if (a.x_out != nullptr) store8(a.x_out + base + 8 * j, v[i]);
+        for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], r[e]);
+        xv[k] = pack8(v);  // x' = bf16(x + add * gate)
+        unpack8(xv[k], v);
+        if (a.x_out != nullptr) st16(a.x_out + base + 8 * j, xv[k]);
       }
+      if (a.center) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, v[i][e]);
-    }
-  }
-  const float mean = a.center ? __fdiv_rn(block_sum(acc, red), float(a.cols)) : 0.f;
-  float acc2 = 0.f;
+        for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, v[e]);
+      } else {
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    if (tid + i * kRowThreads < nvec) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float d = __fsub_rn(v[i][e], mean);
-        acc2 = __fadd_rn(acc2, __fmul_rn(d, d));
+        for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, __fmul_rn(v[e], v[e]));
       }
     }
   }
-  float ssq = block_sum(acc2, red);
-  if (a.pad_cols > 0) ssq = __fadd_rn(ssq, __fmul_rn(float(a.pad_cols), __fmul_rn(mean, mean)));
+  const float first = block_sum(acc, red);
+  float mean = 0.f, ssq = first;
+  if (a.center) {
+    mean = __fdiv_rn(first, float(a.cols));
+    float acc2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      if (tid + k * kRowThreads < nvec) {
+        float v[8];
+        unpack8(xv[k], v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = __fsub_rn(v[e], mean);
+          acc2 = __fadd_rn(acc2, __fmul_rn(d, d));
+        }
+      }
+    }
+    ssq = block_sum(acc2, red);
+    if (a.pad_cols > 0) ssq = __fadd_rn(ssq, __fmul_rn(float(a.pad_cols), __fmul_rn(mean, mean)));
+  }
   const float var = __fdiv_rn(ssq, float(a.cols));
   const float rstd = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, a.eps)));
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int j = tid + i * kRowThreads;
+  for (int k = 0; k < V; ++k) {
+    const int j = tid + k * kRowThreads;
     if (j < nvec) {
       float o[8];
+      unpack8(xv[k], o);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(__fsub_rn(v[i][e], mean), rstd);
+      for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(__fsub_rn(o[e], mean), rstd);
       if (a.w != nullptr) {
         float w[8];
         load8f(a.w + 8 * j, w);
@@ -171,13 +226,13 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(RowNormArgs a) {
         for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(o[e], b[e]);
       }
       if (a.scale != nullptr) {
-        float s[8], h[8];
-        load8f(a.scale + vb + 8 * j, s);
-        load8f(a.shift + vb + 8 * j, h);
+        float sc[8], sh[8];
+        load8f(a.scale + vb + 8 * j, sc);
+        load8f(a.shift + vb + 8 * j, sh);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(__fmul_rn(o[e], __fadd_rn(1.f, s[e])), h[e]);
+        for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(__fmul_rn(o[e], __fadd_rn(1.f, sc[e])), sh[e]);
       }
-      store8(a.y + base + 8 * j, o);
+      st16(a.y + base + 8 * j, pack8(o));
     }
   }
 }
@@ -206,71 +261,93 @@ __device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t bidx, in
   return ((bidx * H + h) * a.tokens + t) * a.head_dim + d;
 }
 
-// RMSNorm of one row (bf16 out), then the rotation of its pairs.
-template <int V>
-__device__ __forceinline__ void norm_rope_row(const QkvArgs& a, const __nv_bfloat16* x, const float* w,
-                                              __nv_bfloat16* out, int64_t bidx, int64_t t, float* red) {
-  const int nvec = a.cols >> 3;
-  const int tid = threadIdx.x;
-  const __nv_bfloat16* xr = x + (bidx * a.tokens + t) * a.cols;
-  float v[V][8];
-  float acc = 0.f;
+// bf16(x * rstd * w), then the rotation of its four pairs by the token's
+// angles (fp64 complex multiply, rounded through fp32), packed.
+__device__ __forceinline__ uint4 norm_rope8(bool rotate, uint4 xp, float rstd, const float* w, const double* cs,
+                                            const double* sn) {
+  float o[8];
+  unpack8(xp, o);
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int j = tid + i * kRowThreads;
-    if (j < nvec) {
-      load8(xr + 8 * j, v[i]);
+  for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(__fmul_rn(o[e], rstd), w[e]);
+  uint4 n = pack8(o);
+  if (!rotate) return n;
+  unpack8(n, o);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, __fmul_rn(v[i][e], v[i][e]));
-    }
+  for (int p = 0; p < 4; ++p) {
+    const double re = o[2 * p], im = o[2 * p + 1];
+    o[2 * p] = __double2float_rn(__dsub_rn(__dmul_rn(re, cs[p]), __dmul_rn(im, sn[p])));
+    o[2 * p + 1] = __double2float_rn(__dadd_rn(__dmul_rn(re, sn[p]), __dmul_rn(im, cs[p])));
   }
-  const float var = __fdiv_rn(block_sum(acc, red), float(a.cols));
-  const float rstd = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, a.eps)));
-  const int half = a.head_dim >> 1;
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int j = tid + i * kRowThreads;
-    if (j < nvec) {
-      const int c = 8 * j;
-      float wv[8], o[8];
-      load8f(w + c, wv);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = bf16_rn(__fmul_rn(__fmul_rn(v[i][e], rstd), wv[e]));
-      if (a.cos != nullptr) {
-        const int p0 = (c % a.head_dim) >> 1;
-        const double* cp = a.cos + t * half + p0;
-        const double* sp = a.sin + t * half + p0;
-        const double2 c01 = *reinterpret_cast<const double2*>(cp);
-        const double2 c23 = *reinterpret_cast<const double2*>(cp + 2);
-        const double2 s01 = *reinterpret_cast<const double2*>(sp);
-        const double2 s23 = *reinterpret_cast<const double2*>(sp + 2);
-        const double cs[4] = {c01.x, c01.y, c23.x, c23.y};
-        const double sn[4] = {s01.x, s01.y, s23.x, s23.y};
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const double re = o[2 * p], im = o[2 * p + 1];
-          o[2 * p] = __double2float_rn(__dsub_rn(__dmul_rn(re, cs[p]), __dmul_rn(im, sn[p])));
-          o[2 * p + 1] = __double2float_rn(__dadd_rn(__dmul_rn(re, sn[p]), __dmul_rn(im, cs[p])));
-        }
-      }
-      store8(out + out_offset(a, bidx, t, c), o);
-    }
-  }
+  return pack8(o);
 }
 
 template <int V>
-__global__ void __launch_bounds__(kRowThreads) qkv_rope_kernel(QkvArgs a) {
-  __shared__ float red[kRowWarps];
+__global__ void __launch_bounds__(kRowThreads, kQkvMinBlocks) qkv_rope_kernel(QkvArgs a) {
+  __shared__ float2 red[kRowWarps];
   const int64_t row = blockIdx.x;
   const int64_t bidx = row / a.tokens, t = row - bidx * a.tokens;
-  norm_rope_row<V>(a, a.xq, a.wq, a.q, bidx, t, red);
-  if (a.xk != nullptr) norm_rope_row<V>(a, a.xk, a.wk, a.k, bidx, t, red);
-  if (a.xv != nullptr) {
-    const int nvec = a.cols >> 3;
-    const __nv_bfloat16* xr = a.xv + row * a.cols;
-    for (int j = threadIdx.x; j < nvec; j += kRowThreads) {
-      const uint4 u = *reinterpret_cast<const uint4*>(xr + 8 * j);
-      *reinterpret_cast<uint4*>(a.v + out_offset(a, bidx, t, 8 * j)) = u;
+  const int nvec = a.cols >> 3;
+  const int tid = threadIdx.x;
+  const int64_t base = row * a.cols;
+  const bool has_k = a.xk != nullptr, rotate = a.cos != nullptr;
+
+  uint4 qv[V], kv[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) {  // q and k rows in flight together
+    const int j = tid + k * kRowThreads;
+    if (j < nvec) {
+      qv[k] = ld16(a.xq + base + 8 * j);
+      if (has_k) kv[k] = ld16(a.xk + base + 8 * j);
+    }
+  }
+  if (a.xv != nullptr) {  // v: a transposing copy
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int j = tid + k * kRowThreads;
+      if (j < nvec) st16(a.v + out_offset(a, bidx, t, 8 * j), ld16(a.xv + base + 8 * j));
+    }
+  }
+  float accq = 0.f, acck = 0.f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    if (tid + k * kRowThreads < nvec) {
+      float v[8];
+      unpack8(qv[k], v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) accq = __fadd_rn(accq, __fmul_rn(v[e], v[e]));
+      if (has_k) {
+        unpack8(kv[k], v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acck = __fadd_rn(acck, __fmul_rn(v[e], v[e]));
+      }
+    }
+  }
+  const float2 sums = block_sum2(accq, acck, red);
+  const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sums.x, float(a.cols)), a.eps)));
+  const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sums.y, float(a.cols)), a.eps)));
+  const int half = a.head_dim >> 1;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int j = tid + k * kRowThreads;
+    if (j < nvec) {
+      const int c = 8 * j;
+      double cs[4] = {0, 0, 0, 0}, sn[4] = {0, 0, 0, 0};
+      if (rotate) {
+        const int p0 = (c % a.head_dim) >> 1;
+        const double2* cp = reinterpret_cast<const double2*>(a.cos + t * half + p0);
+        const double2* sp = reinterpret_cast<const double2*>(a.sin + t * half + p0);
+        const double2 c01 = __ldg(cp), c23 = __ldg(cp + 1), s01 = __ldg(sp), s23 = __ldg(sp + 1);
+        cs[0] = c01.x; cs[1] = c01.y; cs[2] = c23.x; cs[3] = c23.y;
+        sn[0] = s01.x; sn[1] = s01.y; sn[2] = s23.x; sn[3] = s23.y;
+      }
+      const int64_t off = out_offset(a, bidx, t, c);
+      float w[8];
+      load8f(a.wq + c, w);
+      st16(a.q + off, norm_rope8(rotate, qv[k], rq, w, cs, sn));
+      if (has_k) {
+        load8f(a.wk + c, w);
+        st16(a.k + off, norm_rope8(rotate, kv[k], rk, w, cs, sn));
+      }
     }
   }
 }

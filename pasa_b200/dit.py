@@ -167,9 +167,22 @@ def head_to_seq(t: torch.Tensor, group) -> torch.Tensor:
     return recv.permute(1, 0, 2, 3, 4).reshape(B, P * Hl, L // P, D)
 
 
+def head_to_tokens(t: torch.Tensor, group) -> torch.Tensor:
+    """head_to_seq followed by the token-major flatten the output projection
+    reads: [B, H/P, L, D] -> [B, L/P, H*D] with one copy after the all-to-all."""
+    P = dist.get_world_size(group)
+    B, Hl, L, D = t.shape
+    send = t.reshape(B, Hl, P, L // P, D).permute(2, 0, 1, 3, 4).contiguous()
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)         # recv[src] = my tokens of src's heads
+    return recv.permute(1, 3, 0, 2, 4).reshape(B, L // P, P * Hl * D)
+
+
 def pasa_core(density: float) -> Callable:
+    """PASA as the self-attention core; its output is stored token-major so
+    the output projection reads it without a transpose copy."""
     def core(q, k, v):
-        return ops.pisa_pg_attention(q, k, v, density=density)
+        return ops.pisa_pg_attention(q, k, v, density=density, out_layout="bthd")
     return core
 
 
@@ -179,9 +192,8 @@ def _self_attention(q, k, v, w, attn_core, group):
     if group is not None:
         q, k, v = (seq_to_head(t, group) for t in (q, k, v))
     o = attn_core(q.contiguous(), k.contiguous(), v.contiguous())
-    if group is not None:
-        o = head_to_seq(o, group)
-    return F.linear(o.transpose(1, 2).flatten(2, 3), w["o"], w["o_b"])
+    o = head_to_tokens(o, group) if group is not None else o.transpose(1, 2).flatten(2, 3)
+    return F.linear(o, w["o"], w["o_b"])
 
 
 def _cross_attention(cq, text, w, cfg, fused: bool):

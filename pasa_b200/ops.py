@@ -139,6 +139,7 @@ def pisa_pg_attention(
     prompt_token_length: Optional[int] = None,
     *,
     kernel: int = _lib.ATTN_AUTO,
+    out_layout: str = "bhtd",
 ):
     """PASA forward: exact attention on the covariance-aware top-k blocks,
     zero-order + per-group first-order correction on the rest.
@@ -150,9 +151,14 @@ def pisa_pg_attention(
     ``use_random`` adds ``torch.randn_like`` noise to that bias (drawn here,
     on the current CUDA generator, exactly as the reference draws it).
     ``timestep`` and ``prompt_token_length`` are accepted and unused, as in
-    the reference.  Returns a new tensor like ``v``.
+    the reference.  Returns a new [B, H, T, D] tensor like ``v``; with
+    ``out_layout="bthd"`` (bf16, tensor-core kernel) its storage is
+    token-major [B, T, H, D] and the result is the transposed view, so a
+    following ``o.transpose(1, 2).flatten(2, 3)`` costs no copy.
     """
     del timestep, prompt_token_length  # unused by the reference as well
+    if out_layout not in ("bhtd", "bthd"):
+        raise ValueError("out_layout is 'bhtd' or 'bthd'")
     if block_size != 64 or group_size != 32:
         raise ValueError("pasa_b200 supports block_size=64 and group_size=32 (the reference's defaults)")
     _check_qkv(q, k, v)
@@ -165,7 +171,7 @@ def pisa_pg_attention(
         # torch.randn_like(log_bias), log_bias: [B, H, NT] fp32 (:368-370)
         noise = torch.randn((B, H, NT), dtype=torch.float32, device=q.device)
 
-    if verbose:
+    if verbose and out_layout == "bhtd":
         o, st = run_stages(q, k, v, density, scale, use_cov_bias, noise, kernel)
         hn = st.h_norm
         print(f"NT={NT}, N_GROUPS={NG}, GROUP_SIZE={group_size}")
@@ -179,11 +185,15 @@ def pisa_pg_attention(
     with torch.cuda.device(q.device):
         ws_bytes = _lib.workspace_size(B, H, T, K, dcode, NS, block_size, group_size)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-        o = torch.empty_like(v)
-        _lib.check("pasa_forward", lib.pasa_forward(
+        if out_layout == "bthd":
+            o_store = torch.empty((B, T, H, K), dtype=v.dtype, device=v.device)
+            o = o_store.transpose(1, 2)
+        else:
+            o_store = o = torch.empty_like(v)
+        _lib.check("pasa_forward_ex", lib.pasa_forward_ex(
             _stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, T, K, dcode, float(density),
-            float(scale), int(bool(use_cov_bias)), _ptr(noise), ws.data_ptr(), ws_bytes, o.data_ptr(),
-            int(kernel)))
+            float(scale), int(bool(use_cov_bias)), _ptr(noise), ws.data_ptr(), ws_bytes, o_store.data_ptr(),
+            int(kernel), _lib.O_BTHD if out_layout == "bthd" else _lib.O_BHTD))
     return o
 
 
@@ -280,7 +290,6 @@ def _vec(t: Optional[torch.Tensor], cols: int, name: str) -> Optional[torch.Tens
 
 
 DIT_RMSNORM, DIT_LAYERNORM, DIT_LAYERNORM_PADDED = 0, 1, 2
-
 
 def dit_row_norm(x, *, add=None, gate=None, x_out=None, weight=None, bias=None, scale=None, shift=None,
                  eps: float = 1e-6, norm: int = DIT_LAYERNORM, out=None):

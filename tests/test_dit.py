@@ -76,7 +76,8 @@ def _worker(rank, world, port, q):
         hs = dit.seq_to_head(mine, dist.group.WORLD)
         hl = H // world
         ok_fwd = torch.equal(hs, full[:, rank * hl:(rank + 1) * hl])
-        ok_back = torch.equal(dit.head_to_seq(hs, dist.group.WORLD), mine)
+        ok_back = torch.equal(dit.head_to_seq(hs, dist.group.WORLD), mine) and torch.equal(
+            dit.head_to_tokens(hs, dist.group.WORLD), mine.transpose(1, 2).flatten(2, 3))
         out = dit.step(dit.patchify(lat)[:, t0:t1], torch.tensor([500]), txt, (cos[t0:t1], sin[t0:t1]), emb,
                        blocks, cfg, _sdpa, dist.group.WORLD)
         q.put((rank, ok_fwd, ok_back, out))

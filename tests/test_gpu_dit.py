@@ -68,3 +68,22 @@ def test_sparse_step_is_close_to_dense(cuda_device):
     dense = dit.step(x, t, txt, rope, emb, blocks, CFG, lambda q, k, v: dense_attention(q, k, v)).float()
     assert torch.isfinite(sparse).all()
     assert F.cosine_similarity(sparse.flatten(), dense.flatten(), dim=0).item() > 0.99
+
+
+@pytest.mark.parametrize("B,H,T,D", [(2, 3, 1000, 128), (1, 4, 2500, 64)])
+def test_token_major_output_equals_head_major(cuda_device, B, H, T, D):
+    """out_layout="bthd" stores the same values token-major (pasa_forward_ex)."""
+    from pasa_b200 import pisa_pg_attention
+    g = torch.Generator().manual_seed(T + D)
+    q, k, v = (torch.randn((B, H, T, D), generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(3))
+    a = pisa_pg_attention(q, k, v, density=0.2)
+    b = pisa_pg_attention(q, k, v, density=0.2, out_layout="bthd")
+    assert b.shape == a.shape and b.transpose(1, 2).is_contiguous()
+    assert torch.equal(a, b)
+
+
+def test_token_major_output_needs_the_tensor_core_kernel(cuda_device):
+    from pasa_b200 import pisa_pg_attention
+    q = torch.randn((1, 2, 256, 64), device=cuda_device)
+    with pytest.raises(ValueError):                 # fp32 runs the CUDA-core kernel: [B*H, T, D] only
+        pisa_pg_attention(q, q, q, density=0.5, out_layout="bthd")
