@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks in the DiT step (40 = the full model)")
     ap.add_argument("--dit-density", type=float, default=0.1)
     ap.add_argument("--dit-frames", type=int, default=0, help="latent frames (0 = 21, the 81-frame video)")
+    ap.add_argument("--dit-exchange", default="peer", choices=["peer", "nccl"],
+                    help="Ulysses exchange with N > 1: kernels storing into peer memory (fused), or NCCL all-to-all")
     ap.add_argument("--dit-torch", action="store_true",
                     help="DiT step with torch elementwise ops instead of the row kernels (comparison)")
     return ap.parse_args()
@@ -264,18 +266,19 @@ def run_dit(args):
 
     attn_events, a2a_events = [], []
 
-    def timed(fn):
-        def run(t, g):
+    def timed(fn, events):
+        def run(*a, **kw):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            r = fn(t, g)
+            r = fn(*a, **kw)
             e1.record(stream)
-            a2a_events.append((e0, e1))
+            events.append((e0, e1))
             return r
         return run
 
     # time the Ulysses all-to-alls (resharding copies included)
-    dit.seq_to_head, dit.head_to_tokens = timed(dit.seq_to_head), timed(dit.head_to_tokens)
+    dit.seq_to_head = timed(dit.seq_to_head, a2a_events)
+    dit.head_to_tokens = timed(dit.head_to_tokens, a2a_events)
 
     def core(q, k, v):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -286,18 +289,35 @@ def run_dit(args):
         return o
 
     fused = not args.dit_torch
+    exchange = None
+    if world > 1 and fused and args.dit_exchange == "peer":
+        from pasa_b200.exchange import UlyssesPeerExchange
 
-    def step():
-        return dit.step(lat_d, timestep, text_d, rope, embed, blocks, cfg, core, group, fused=fused)
+        exchange = UlyssesPeerExchange(group, dev, cfg.heads, cfg.head_dim, t1 - t0)
+        # time the two fused exchanges like the all-to-alls (kernel + its barrier)
+        exchange.attention = timed(exchange.attention, attn_events)
+        exchange.scatter_qkv = timed(exchange.scatter_qkv, a2a_events)
+
+    def step(ex=exchange):
+        return dit.step(lat_d, timestep, text_d, rope, embed, blocks, cfg, core, group, fused=fused, exchange=ex)
 
     def e2e_step():
         # the public call with host buffers: latents and text in, predicted patches out
         lat_g = lat_h.to(dev, non_blocking=True)
         text_g = text_h.to(dev, non_blocking=True)
-        out = dit.step(lat_g, timestep, text_g, rope, embed, blocks, cfg, core, group, fused=fused)
+        out = dit.step(lat_g, timestep, text_g, rope, embed, blocks, cfg, core, group, fused=fused,
+                       exchange=exchange)
         out_h.copy_(out, non_blocking=True)
 
     with torch.no_grad():
+        if exchange is not None:
+            # the fused exchange moves the same values as the all-to-alls:
+            # the step's output must be bit-identical to the NCCL path's
+            same = torch.equal(step(), step(ex=None))
+            flags = torch.tensor([0 if same else 1], device=dev)
+            dist.all_reduce(flags)
+            if int(flags.item()):
+                raise SystemExit("peer-memory exchange differs from the NCCL all-to-all path")
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
@@ -356,9 +376,13 @@ def run_dit(args):
                        "ffn": Fd, "tokens": tokens, "text_len": Lt, "density": cfg.density,
                        "parallelism": f"ulysses{world}" if world > 1 else "none",
                        "elementwise": "row kernels (pasa_dit_row_norm, pasa_dit_qkv_rope)" if fused else "torch ops",
+                       "exchange": (None if world == 1 else
+                                    "fused peer-memory scatter (qkv_rope_scatter + forward_scatter, NCCL barrier)"
+                                    if exchange is not None else "NCCL all-to-all"),
                        "l2": "activations 0.77 GB per tensor > 126 MB L2; no flush"},
             "kernels_ms": {"pasa_attention_per_step": attn_ms, "attention_share": attn_ms / ms_step,
-                           "ulysses_all_to_all_per_step": a2a_ms if world > 1 else 0.0},
+                           ("ulysses_qkv_scatter_per_step" if exchange is not None else
+                            "ulysses_all_to_all_per_step"): a2a_ms if world > 1 else 0.0},
             "gemm_tflop_per_step": gemm / 1e12,
             "e2e": None if e2e_ms is None else {
                 "value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": (nbytes(lat_h) + nbytes(text_h)) * world,
@@ -370,6 +394,8 @@ def run_dit(args):
             "gpu_launches": ((9 * cfg.layers + 1) if fused else 3 * cfg.layers) * args.steps,
         }
         print(json.dumps(line), flush=True)
+    if exchange is not None:
+        exchange.close()
     if world > 1:
         dist.destroy_process_group()
 

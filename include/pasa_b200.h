@@ -288,6 +288,52 @@ PASA_API int pasa_dit_qkv_rope(void* stream, const void* xq, const void* xk, con
               int64_t batch, int64_t tokens, int heads, int head_dim, float eps, int head_major,
               void* q, void* k, void* v);
 
+/*
+ * Fused Ulysses exchange of the DiT step (no reference counterpart: the
+ * reference has no collectives).  With P ranks, rank r holds tokens
+ * [r*L, (r+1)*L) of the sequence (L = tokens per rank) and attends heads
+ * [r*H/P, (r+1)*H/P).  Peer buffers are allocated by the library and shared
+ * through CUDA IPC handles (PASA_PEER_HANDLE_BYTES each, exchanged by the
+ * caller, e.g. an all-gather); kernels store into them over NVLink with plain
+ * peer stores.  The caller orders the kernels across ranks (a stream-ordered
+ * barrier collective after each scatter, before the buffers are read).
+ */
+#define PASA_PEER_HANDLE_BYTES 64
+
+/* cudaMalloc `bytes` and export its IPC handle (host buffer of
+ * PASA_PEER_HANDLE_BYTES). */
+PASA_API int pasa_peer_alloc(size_t bytes, void** ptr, void* handle);
+PASA_API int pasa_peer_free(void* ptr);
+/* Map another process's buffer from its handle (same node); pasa_peer_close
+ * unmaps it. */
+PASA_API int pasa_peer_open(const void* handle, void** ptr);
+PASA_API int pasa_peer_close(void* ptr);
+
+/*
+ * pasa_dit_qkv_rope for one batch entry, with the head-major outputs
+ * scattered to the ranks that attend them: the row of head h and local
+ * token t goes to rank h / (H/P), whose buffer peer_table[rank] holds
+ * [3][H/P][P*tokens][D] (q, k, v), at token rank*tokens + t.  peer_table is
+ * a DEVICE array of P pointers (this rank's own buffer included).
+ * Replaces the producer + sequence-to-head all-to-all.
+ */
+PASA_API int pasa_dit_qkv_rope_scatter(void* stream, const void* xq, const void* xk, const void* xv,
+              const float* wq, const float* wk, const double* cos, const double* sin,
+              int64_t tokens, int heads, int head_dim, float eps,
+              void* const* peer_table, int n_ranks, int rank);
+
+/*
+ * pasa_forward (B = 1, bf16, tcgen05) on this rank's H_local heads over all T
+ * tokens, with every output row stored at its token's owner: token t goes to
+ * rank t / (T/P), whose buffer o_peer_table[rank] holds [T/P][heads_total][D]
+ * (token-major, the output projection's layout), at head head0 + h.
+ * Replaces the attention + head-to-sequence all-to-all.
+ */
+PASA_API int pasa_forward_scatter(void* stream, const void* q, const void* k, const void* v,
+              int64_t H_local, int64_t T, int D, double density, float scale, int use_cov_bias,
+              const float* noise, void* workspace, size_t workspace_bytes,
+              void* const* o_peer_table, int n_ranks, int64_t head0, int64_t heads_total, int kernel);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,11 +36,14 @@ DEVERR_WAIT_TIMEOUT = 0x1
 O_BHTD = 0
 O_BTHD = 1
 
+PEER_HANDLE_BYTES = 64
+
 EXPORTS = (
     "pasa_abi_version", "pasa_status_string", "pasa_derive", "pasa_workspace_size", "pasa_prep",
     "pasa_select", "pasa_attn", "pasa_forward", "pasa_forward_noalloc", "pasa_place",
     "pasa_forward_host_workspace_size", "pasa_forward_host", "pasa_dense_attn",
-    "pasa_dit_row_norm", "pasa_dit_qkv_rope", "pasa_forward_ex",
+    "pasa_dit_row_norm", "pasa_dit_qkv_rope", "pasa_forward_ex", "pasa_peer_alloc", "pasa_peer_free",
+    "pasa_peer_open", "pasa_peer_close", "pasa_dit_qkv_rope_scatter", "pasa_forward_scatter",
 )
 
 _lib = None
@@ -80,6 +83,14 @@ def load() -> ctypes.CDLL:
         "pasa_dense_attn": (c_int, [P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, P, P]),
         "pasa_forward_ex": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float,
                                     c_int, P, P, c_size_t, P, c_int, c_int]),
+        "pasa_peer_alloc": (c_int, [c_size_t, POINTER(c_void_p), P]),
+        "pasa_peer_free": (c_int, [P]),
+        "pasa_peer_open": (c_int, [P, POINTER(c_void_p)]),
+        "pasa_peer_close": (c_int, [P]),
+        "pasa_dit_qkv_rope_scatter": (c_int, [P, P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float, P, c_int,
+                                              c_int]),
+        "pasa_forward_scatter": (c_int, [P, P, P, P, c_int64, c_int64, c_int, c_double, c_float, c_int, P, P,
+                                         c_size_t, P, c_int, c_int64, c_int64, c_int]),
         "pasa_dit_row_norm": (c_int, [P, P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_float, c_int, P]),
         "pasa_dit_qkv_rope": (c_int, [P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, c_int,
                                       P, P, P]),

@@ -114,6 +114,11 @@ struct Params {
   uint32_t* err;
   int dense;  // every key block selected for every query block (sel_mask unused, no phase 2)
   int64_t o_heads;  // 0: o is [B*H, T, D]; H > 0: o is [B, T, H, D] (token-major, bh = b*H + h)
+  // scatter mode (o_npeer > 0, B = 1): the row of local head bh and token t
+  // goes to o_peer[t / o_tokens] at [(t % o_tokens) * o_heads_total + o_head0 + bh]
+  __nv_bfloat16* const* o_peer;
+  int o_npeer;
+  int64_t o_tokens, o_heads_total, o_head0;
 };
 
 // Optional step tracer (compile with -DPASA_TRACE): one CTA, chosen with
@@ -690,10 +695,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         const bool store = t < P.T;
         const float denom = l_tot + g_tot * fast_exp2(m_true - m_used);
         const float inv = 1.0f / denom;
-        const int64_t orow_idx = P.o_heads > 0
-                                     ? ((bh / P.o_heads) * P.T + t) * P.o_heads + bh % P.o_heads
-                                     : bh * P.T + t;
-        __nv_bfloat16* orow = P.o + orow_idx * D + set * DH;
+        __nv_bfloat16* orow;
+        if (P.o_npeer > 0) {
+          const int64_t ts = store ? t : 0;
+          const int64_t dst = ts / P.o_tokens;
+          orow = P.o_peer[dst] + ((ts - dst * P.o_tokens) * P.o_heads_total + P.o_head0 + bh) * D + set * DH;
+        } else {
+          const int64_t orow_idx = P.o_heads > 0
+                                       ? ((bh / P.o_heads) * P.T + t) * P.o_heads + bh % P.o_heads
+                                       : bh * P.T + t;
+          orow = P.o + orow_idx * D + set * DH;
+        }
 #pragma unroll
         for (int c0 = 0; c0 < DH; c0 += 16) {
           uint32_t v[16];
@@ -709,6 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             reinterpret_cast<uint4*>(orow + c0)[1] = out[1];
           }
         }
+        if (P.o_npeer > 0) __threadfence_system();  // peer stores done before the kernel ends
       }
     }
     if (!ok) report(P.err);
@@ -754,7 +767,8 @@ bool make_map(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t bat
 template <int D>
 cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const void* v, const void* kc,
                         const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
-                        float scale, void* o, uint32_t* err, int dense, int64_t o_heads) {
+                        float scale, void* o, uint32_t* err, int dense, int64_t o_heads,
+                        const OutScatter& sc) {
   using C = Cfg<D>;
   const int64_t NT = cdiv(T_len, kBlock), NG = cdiv(NT, kGroup), NTP = NG * kGroup;
   if (NT > kMaxNT) return cudaErrorInvalidValue;
@@ -767,6 +781,11 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
   p.T = T_len; p.NT = NT; p.NG = NG; p.NTP = NTP; p.scale = scale;
   p.o = static_cast<__nv_bfloat16*>(o); p.sel_mask = mask; p.err = err; p.dense = dense;
   p.o_heads = o_heads;
+  p.o_peer = reinterpret_cast<__nv_bfloat16* const*>(sc.peer);
+  p.o_npeer = sc.npeer;
+  p.o_tokens = sc.tokens;
+  p.o_heads_total = sc.heads_total;
+  p.o_head0 = sc.head0;
   auto kern = attn_tc_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -779,9 +798,11 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
 
 cudaError_t launch_attn_tc(cudaStream_t st, int D, const void* q, const void* k, const void* v, const void* kc,
                            const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
-                           int64_t /*NS*/, float scale, void* o, uint32_t* err, int dense, int64_t o_heads) {
-  if (D == 64) return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads);
-  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads);
+                           int64_t /*NS*/, float scale, void* o, uint32_t* err, int dense, int64_t o_heads,
+                           const OutScatter& sc) {
+  if (D == 64)
+    return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads, sc);
+  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads, sc);
 }
 
 }  // namespace pasa

@@ -17,7 +17,7 @@ cudaError_t launch_attn_simt(cudaStream_t, int, int, const void*, const void*, c
                              int64_t, float, void*);
 cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const void*, const void*, const void*,
                            const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*, int,
-                           int64_t);
+                           int64_t, const OutScatter&);
 cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
                          int64_t, int64_t, int64_t, int);
 int dit_max_cols();
@@ -25,7 +25,7 @@ cudaError_t launch_row_norm(cudaStream_t, const void*, const void*, const float*
                             const float*, const float*, int64_t, int64_t, int, float, int, int, void*);
 cudaError_t launch_qkv_rope(cudaStream_t, const void*, const void*, const void*, const float*, const float*,
                             const double*, const double*, int64_t, int64_t, int, int, float, int, void*, void*,
-                            void*);
+                            void*, void* const*, int, int);
 }  // namespace pasa
 
 using namespace pasa;
@@ -160,18 +160,20 @@ int pasa_select(void* stream, const void* qc, const void* kc, const float* h_nor
 namespace {
 
 // pasa_attn with the output layout: o_heads = 0 writes [B*H, T, D], o_heads =
-// H > 0 writes [B, T, H, D] (tensor-core kernel only).
+// H > 0 writes [B, T, H, D]; sc.npeer > 0 scatters the rows to the token
+// owners' buffers instead of o (tensor-core kernel only for both).
 int attn_dispatch(void* stream, const void* q, const void* k, const void* v, const void* kc, const void* vc,
                   const void* h_group, const int32_t* indices, const uint32_t* sel_mask, int64_t BH, int64_t T,
                   int D, int dtype, float scale, int64_t ns, void* o, uint32_t* err_word, int kernel,
-                  int64_t o_heads) {
+                  int64_t o_heads, const OutScatter& sc = OutScatter{}) {
   int st = check_common(BH, T, D, dtype);
   if (st) return st;
   const int64_t NT = cdiv(T, kBlock), NG = cdiv(NT, kGroup);
   if (ns < 1 || ns > NT) return PASA_ERR_SHAPE;
-  if (!q || !k || !v || !kc || !vc || !h_group || !sel_mask || !o) return PASA_ERR_NULL;
+  const bool scatter = sc.npeer > 0;
+  if (!q || !k || !v || !kc || !vc || !h_group || !sel_mask || (!o && !scatter)) return PASA_ERR_NULL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(kc) || !aligned16(vc) ||
-      !aligned16(h_group) || !aligned16(o))
+      !aligned16(h_group) || (!scatter && !aligned16(o)))
     return PASA_ERR_ALIGN;
   if (!std::isfinite(scale)) return PASA_ERR_SHAPE;
   if (kernel == PASA_ATTN_AUTO) kernel = (dtype == PASA_BF16) ? PASA_ATTN_TCGEN05 : PASA_ATTN_SIMT;
@@ -181,10 +183,10 @@ int attn_dispatch(void* stream, const void* q, const void* k, const void* v, con
   if (kernel == PASA_ATTN_TCGEN05) {
     if (dtype != PASA_BF16) return PASA_ERR_DTYPE;
     return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word, 0,
-                                      o_heads));
+                                      o_heads, sc));
   }
   if (kernel != PASA_ATTN_SIMT) return PASA_ERR_UNSUPPORTED;
-  if (o_heads > 0) return PASA_ERR_UNSUPPORTED;  // the CUDA-core kernel writes [B*H, T, D] only
+  if (o_heads > 0 || scatter) return PASA_ERR_UNSUPPORTED;  // the CUDA-core kernel writes [B*H, T, D] only
   if (!indices) return PASA_ERR_NULL;
   if (NG > 64) return PASA_ERR_SHAPE;  // the CUDA-core kernel keeps one word per group in shared memory
   return cuda_status(launch_attn_simt(s, dtype, D, q, k, v, kc, vc, h_group, indices, sel_mask, BH, T, ns, scale,
@@ -207,15 +209,17 @@ int pasa_forward(void* stream, const void* q, const void* k, const void* v, int6
                          workspace_bytes, o, kernel, PASA_O_BHTD);
 }
 
-int pasa_forward_ex(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T,
-                    int D, int dtype, double density, float scale, int use_cov_bias, const float* noise,
-                    void* workspace, size_t workspace_bytes, void* o, int kernel, int o_layout) {
+namespace {
+
+// prep -> select -> attention on one workspace (pasa_forward_ex, pasa_forward_scatter).
+int forward_impl(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
+                 int dtype, double density, float scale, int use_cov_bias, const float* noise, void* workspace,
+                 size_t workspace_bytes, void* o, int kernel, int64_t o_heads, const OutScatter& sc) {
   if (B < 1 || H < 1) return PASA_ERR_SHAPE;
-  if (o_layout != PASA_O_BHTD && o_layout != PASA_O_BTHD) return PASA_ERR_UNSUPPORTED;
   int st = check_common(B * H, T, D, dtype);
   if (st) return st;
   if (!std::isfinite(density)) return PASA_ERR_DENSITY;
-  if (!q || !k || !v || !o) return PASA_ERR_NULL;
+  if (!q || !k || !v || (!o && sc.npeer == 0)) return PASA_ERR_NULL;
   const int64_t BH = B * H, NT = cdiv(T, kBlock);
   const int64_t NS = top_k_of(density, NT);
   const Layout L = make_layout(BH, T, D, esize_of(dtype), NS);
@@ -237,8 +241,37 @@ int pasa_forward_ex(void* stream, const void* q, const void* k, const void* v, i
   if ((st = pasa_select(stream, qc, kc, hn, noise, BH, NT, D, dtype, scale, use_cov_bias, NS, idx, mask)))
     return st;
   if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
-  return attn_dispatch(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel,
-                       o_layout == PASA_O_BTHD ? H : 0);
+  return attn_dispatch(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel, o_heads,
+                       sc);
+}
+
+}  // namespace
+
+int pasa_forward_ex(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T,
+                    int D, int dtype, double density, float scale, int use_cov_bias, const float* noise,
+                    void* workspace, size_t workspace_bytes, void* o, int kernel, int o_layout) {
+  if (o_layout != PASA_O_BHTD && o_layout != PASA_O_BTHD) return PASA_ERR_UNSUPPORTED;
+  if (!o) return PASA_ERR_NULL;
+  return forward_impl(stream, q, k, v, B, H, T, D, dtype, density, scale, use_cov_bias, noise, workspace,
+                      workspace_bytes, o, kernel, o_layout == PASA_O_BTHD ? H : 0, OutScatter{});
+}
+
+int pasa_forward_scatter(void* stream, const void* q, const void* k, const void* v, int64_t H_local, int64_t T,
+                         int D, double density, float scale, int use_cov_bias, const float* noise, void* workspace,
+                         size_t workspace_bytes, void* const* o_peer_table, int n_ranks, int64_t head0,
+                         int64_t heads_total, int kernel) {
+  if (n_ranks < 1 || n_ranks > 64 || T < 1 || T % n_ranks != 0) return PASA_ERR_SHAPE;
+  if (H_local < 1 || head0 < 0 || heads_total < head0 + H_local) return PASA_ERR_SHAPE;
+  if (!o_peer_table) return PASA_ERR_NULL;
+  if (kernel != PASA_ATTN_AUTO && kernel != PASA_ATTN_TCGEN05) return PASA_ERR_UNSUPPORTED;
+  OutScatter sc;
+  sc.peer = o_peer_table;
+  sc.npeer = n_ranks;
+  sc.tokens = T / n_ranks;
+  sc.heads_total = heads_total;
+  sc.head0 = head0;
+  return forward_impl(stream, q, k, v, 1, H_local, T, D, PASA_BF16, density, scale, use_cov_bias, noise, workspace,
+                      workspace_bytes, nullptr, PASA_ATTN_TCGEN05, 0, sc);
 }
 
 int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, int64_t BH, int64_t T, int D,
@@ -252,7 +285,7 @@ int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, i
   if ((st = check_device())) return st;
   // the block statistics are not read in dense mode; q stands in for their (unused) tensor maps
   return cuda_status(launch_attn_tc(static_cast<cudaStream_t>(stream), D, q, k, v, q, q, q, nullptr, BH, T,
-                                    cdiv(T, kBlock), scale, o, err_word, 1, 0));
+                                    cdiv(T, kBlock), scale, o, err_word, 1, 0, OutScatter{}));
 }
 
 int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal, int64_t cfg, int64_t H,
@@ -307,7 +340,26 @@ int pasa_dit_qkv_rope(void* stream, const void* xq, const void* xk, const void* 
   if (st) return st;
   return cuda_status(launch_qkv_rope(static_cast<cudaStream_t>(stream), xq, xk, xv, wq, wk, cos, sin, batch, tokens,
                                      int(cols), head_dim, eps, head_major ? 1 : 0, q, xk ? k : nullptr,
-                                     xv ? v : nullptr));
+                                     xv ? v : nullptr, nullptr, 0, 0));
+}
+
+int pasa_dit_qkv_rope_scatter(void* stream, const void* xq, const void* xk, const void* xv, const float* wq,
+                              const float* wk, const double* cos, const double* sin, int64_t tokens, int heads,
+                              int head_dim, float eps, void* const* peer_table, int n_ranks, int rank) {
+  if (tokens < 1 || heads < 1 || head_dim < 8 || head_dim % 8 != 0) return PASA_ERR_SHAPE;
+  const int64_t cols = int64_t(heads) * head_dim;
+  if (cols > dit_max_cols() || tokens * n_ranks > INT32_MAX) return PASA_ERR_SHAPE;
+  if (n_ranks < 1 || n_ranks > 64 || heads % n_ranks != 0 || rank < 0 || rank >= n_ranks) return PASA_ERR_SHAPE;
+  if (!std::isfinite(eps) || eps < 0.f) return PASA_ERR_SHAPE;
+  if (!xq || !xk || !xv || !wq || !wk || !peer_table || (cos == nullptr) != (sin == nullptr)) return PASA_ERR_NULL;
+  const void* ptrs[] = {xq, xk, xv, wq, wk, cos, sin};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return PASA_ERR_ALIGN;
+  int st = check_device();
+  if (st) return st;
+  return cuda_status(launch_qkv_rope(static_cast<cudaStream_t>(stream), xq, xk, xv, wq, wk, cos, sin, 1, tokens,
+                                     int(cols), head_dim, eps, 1, nullptr, nullptr, nullptr, peer_table, n_ranks,
+                                     rank));
 }
 
 }  // extern "C"

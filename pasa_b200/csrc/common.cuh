@@ -10,6 +10,14 @@
 
 namespace pasa {
 
+// Scatter of the attention output to the ranks that own its tokens (the
+// fused head-to-sequence exchange); npeer = 0 means a plain store.
+struct OutScatter {
+  void* const* peer = nullptr;  // device table of npeer token-major buffers
+  int npeer = 0;
+  int64_t tokens = 0, heads_total = 0, head0 = 0;
+};
+
 constexpr int kBlock = 64;   // tokens per block (BT of the reference)
 constexpr int kGroup = 32;   // blocks per correction group (GROUP_SIZE)
 constexpr float kLog2e = 1.44269504f;  // group_pisa_attention.py:162

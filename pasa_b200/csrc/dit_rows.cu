@@ -252,13 +252,24 @@ struct QkvArgs {
   int cols, head_dim;
   float eps;
   int head_major;           // 1: [B, H, tokens, D]; 0: [B, tokens, H*D]
+  __nv_bfloat16* const* peer;  // scatter mode: device table of the ranks' [3][H/P][P*tokens][D] buffers
+  int npeer;                // 0: write q, k, v; P > 0: scatter to the P ranks
+  int rank;                 // scatter mode: this rank (its tokens start at rank * tokens)
 };
 
-__device__ __forceinline__ int64_t out_offset(const QkvArgs& a, int64_t bidx, int64_t t, int c) {
-  if (!a.head_major) return (bidx * a.tokens + t) * a.cols + c;
+// Destination of the 8 values at column c of token t (which: 0 q, 1 k, 2 v).
+__device__ __forceinline__ __nv_bfloat16* out_ptr(const QkvArgs& a, int which, int64_t bidx, int64_t t, int c) {
   const int h = c / a.head_dim, d = c - h * a.head_dim;
+  if (a.npeer > 0) {
+    const int hl = (a.cols / a.head_dim) / a.npeer;
+    const int dst = h / hl, hh = h - dst * hl;
+    const int64_t rows = a.tokens * a.npeer;
+    return a.peer[dst] + ((int64_t(which) * hl + hh) * rows + int64_t(a.rank) * a.tokens + t) * a.head_dim + d;
+  }
+  __nv_bfloat16* base = which == 0 ? a.q : (which == 1 ? a.k : a.v);
+  if (!a.head_major) return base + (bidx * a.tokens + t) * a.cols + c;
   const int64_t H = a.cols / a.head_dim;
-  return ((bidx * H + h) * a.tokens + t) * a.head_dim + d;
+  return base + ((bidx * H + h) * a.tokens + t) * a.head_dim + d;
 }
 
 // bf16(x * rstd * w), then the rotation of its four pairs by the token's
@@ -304,7 +315,7 @@ __global__ void __launch_bounds__(kRowThreads, kQkvMinBlocks) qkv_rope_kernel(Qk
 #pragma unroll
     for (int k = 0; k < V; ++k) {
       const int j = tid + k * kRowThreads;
-      if (j < nvec) st16(a.v + out_offset(a, bidx, t, 8 * j), ld16(a.xv + base + 8 * j));
+      if (j < nvec) st16(out_ptr(a, 2, bidx, t, 8 * j), ld16(a.xv + base + 8 * j));
     }
   }
   float accq = 0.f, acck = 0.f;
@@ -340,16 +351,18 @@ __global__ void __launch_bounds__(kRowThreads, kQkvMinBlocks) qkv_rope_kernel(Qk
         cs[0] = c01.x; cs[1] = c01.y; cs[2] = c23.x; cs[3] = c23.y;
         sn[0] = s01.x; sn[1] = s01.y; sn[2] = s23.x; sn[3] = s23.y;
       }
-      const int64_t off = out_offset(a, bidx, t, c);
       float w[8];
       load8f(a.wq + c, w);
-      st16(a.q + off, norm_rope8(rotate, qv[k], rq, w, cs, sn));
+      st16(out_ptr(a, 0, bidx, t, c), norm_rope8(rotate, qv[k], rq, w, cs, sn));
       if (has_k) {
         load8f(a.wk + c, w);
-        st16(a.k + off, norm_rope8(rotate, kv[k], rk, w, cs, sn));
+        st16(out_ptr(a, 1, bidx, t, c), norm_rope8(rotate, kv[k], rk, w, cs, sn));
       }
     }
   }
+  // peer stores are complete at system scope before the kernel's end (the
+  // caller's barrier collective follows it on the stream)
+  if (a.npeer > 0) __threadfence_system();
 }
 
 int vectors_per_thread(int cols) { return int(cdiv(cols / 8, kRowThreads)); }
@@ -393,8 +406,12 @@ cudaError_t launch_row_norm(cudaStream_t stream, const void* x, const void* add,
 
 cudaError_t launch_qkv_rope(cudaStream_t stream, const void* xq, const void* xk, const void* xv, const float* wq,
                             const float* wk, const double* cos, const double* sin, int64_t batch, int64_t tokens,
-                            int cols, int head_dim, float eps, int head_major, void* q, void* k, void* v) {
+                            int cols, int head_dim, float eps, int head_major, void* q, void* k, void* v,
+                            void* const* peer, int npeer, int rank) {
   QkvArgs a;
+  a.peer = reinterpret_cast<__nv_bfloat16* const*>(peer);
+  a.npeer = npeer;
+  a.rank = rank;
   a.xq = static_cast<const __nv_bfloat16*>(xq);
   a.xk = static_cast<const __nv_bfloat16*>(xk);
   a.xv = static_cast<const __nv_bfloat16*>(xv);

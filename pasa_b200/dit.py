@@ -246,11 +246,13 @@ Pending = Optional[Tuple[torch.Tensor, torch.Tensor]]
 
 
 def block_forward_fused(x: torch.Tensor, pending: Pending, text: torch.Tensor, temb: torch.Tensor, rope, w: dict,
-                        cfg: DiTConfig, attn_core: Callable, group=None) -> Tuple[torch.Tensor, Pending]:
+                        cfg: DiTConfig, attn_core: Callable, group=None, exchange=None) -> Tuple[torch.Tensor, Pending]:
     """One block with the row kernels; ``x`` (bf16, contiguous) is updated in
     place.  ``pending`` = (ffn output, its gate) of the previous block, whose
     residual update is folded into this block's first norm; the block returns
-    its own pending pair."""
+    its own pending pair.  With ``exchange`` (a ``UlyssesPeerExchange``) the
+    sequence<->head exchange is done by the producer and the attention
+    kernels themselves over peer memory, and PASA runs at ``cfg.density``."""
     mods = (w["scale_shift_table"] + temb.float()).chunk(6, dim=1)
     shift, scale, gate, c_shift, c_scale, c_gate = (m.contiguous() for m in mods)
     add, add_gate = pending if pending is not None else (None, None)
@@ -258,10 +260,14 @@ def block_forward_fused(x: torch.Tensor, pending: Pending, text: torch.Tensor, t
     # 1. (previous FFN residual) + LayerNorm + modulation -> self-attention
     h = ops.dit_row_norm(x, add=add, gate=add_gate, x_out=x if add is not None else None, scale=scale,
                          shift=shift, eps=cfg.eps)
-    q, k, v = ops.dit_qkv_rope(F.linear(h, w["q"], w["q_b"]), F.linear(h, w["k"], w["k_b"]),
-                               F.linear(h, w["v"], w["v_b"]), w["norm_q_f"], w["norm_k_f"], rope[0], rope[1],
-                               cfg.heads, cfg.eps, head_major=True)
-    o = _self_attention(q, k, v, w, attn_core, group)
+    xq, xk, xv = F.linear(h, w["q"], w["q_b"]), F.linear(h, w["k"], w["k_b"]), F.linear(h, w["v"], w["v_b"])
+    if exchange is not None:
+        q, k, v = exchange.scatter_qkv(xq, xk, xv, w["norm_q_f"], w["norm_k_f"], rope[0], rope[1], cfg.eps)
+        o = F.linear(exchange.attention(q, k, v, cfg.density), w["o"], w["o_b"])
+    else:
+        q, k, v = ops.dit_qkv_rope(xq, xk, xv, w["norm_q_f"], w["norm_k_f"], rope[0], rope[1], cfg.heads, cfg.eps,
+                                   head_major=True)
+        o = _self_attention(q, k, v, w, attn_core, group)
 
     # 2. gated residual + affine LayerNorm -> cross-attention
     h = ops.dit_row_norm(x, add=o, gate=gate, x_out=x, weight=w["norm2_w"], bias=w["norm2_b"], eps=cfg.eps)
@@ -333,13 +339,15 @@ def condition(e: dict, timestep: torch.Tensor, text_embed: torch.Tensor):
 
 
 def step(latents_local: torch.Tensor, timestep: torch.Tensor, text_embed: torch.Tensor, rope, embed: dict,
-         blocks: List[dict], cfg: DiTConfig, attn_core: Callable, group=None, fused: bool = False) -> torch.Tensor:
+         blocks: List[dict], cfg: DiTConfig, attn_core: Callable, group=None, fused: bool = False,
+         exchange=None) -> torch.Tensor:
     """One denoising step (the transformer forward of the reference's
     WanTransformer3DModel_Sparse.forward, svg/models/wan/custom_models.py:115-200)
     on this rank's tokens: patch embedding, condition embedder, every block,
     output norm and projection.  ``latents_local`` holds this rank's patches
     [B, L_local, c*4]; returns the predicted patches [B, L_local, c*4].
-    ``fused`` selects the row-kernel path (bf16 CUDA tensors)."""
+    ``fused`` selects the row-kernel path (bf16 CUDA tensors); ``exchange``
+    (with ``fused``) replaces the NCCL all-to-alls by the peer-memory scatter."""
     temb, tproj, text = condition(embed, timestep, text_embed)
     x = F.linear(latents_local.to(embed["patch"].dtype), embed["patch"], embed["patch_b"])
     shift, scale = (embed["out_table"] + temb.unsqueeze(1)).chunk(2, dim=1)
@@ -347,7 +355,7 @@ def step(latents_local: torch.Tensor, timestep: torch.Tensor, text_embed: torch.
         x = x.contiguous()
         pending: Pending = None
         for w in blocks:
-            x, pending = block_forward_fused(x, pending, text, tproj, rope, w, cfg, attn_core, group)
+            x, pending = block_forward_fused(x, pending, text, tproj, rope, w, cfg, attn_core, group, exchange)
         add, add_gate = pending if pending is not None else (None, None)
         h = ops.dit_row_norm(x, add=add, gate=add_gate, x_out=x if add is not None else None,
                              scale=scale.contiguous(), shift=shift.contiguous(), eps=cfg.eps)
