@@ -372,6 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // step n-2 holds that step's scores in registers (s_free)
         ok = mbar_wait_bounded(q_full, 0, kPollLimit);
         const uint32_t q_base = smem_u32(sm + C::kOffQ);
+        // Descriptors of the k-th K16 slice are the base descriptor plus the
+        // slice's byte offset >> 4: the address field is the low 14 bits
+        // (shared addresses < 256 KB), so the add never carries out of it.
+        const uint64_t qd0 = umma_desc_sw128(q_base, 16, 1024);
         for (int64_t n = 0; n < total && ok; ++n) {
           if (n >= 2) {
             const int64_t m = n - 2;
@@ -386,23 +390,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           tc_fence_after();
           const uint32_t tS = tmem + C::kColS0 + 128u * uint32_t(n & 1);
           if (n < nP) {  // S = Q . [K_j0; K_j1]^T, N = 128
-            const uint32_t kst = smem_u32(sm + C::kOffK + int(n % C::kSK) * C::kPairBytes);
+            const uint64_t kd0 =
+                umma_desc_sw128(smem_u32(sm + C::kOffK + int(n % C::kSK) * C::kPairBytes), 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
-              const int bx = kk / 4, ko = (kk % 4) * 32;
-              const uint64_t ad = umma_desc_sw128(q_base + bx * C::kRowBox + ko, 16, 1024);
-              const uint64_t bd = umma_desc_sw128(kst + bx * C::kRowBox + ko, 16, 1024);
-              mma_ss(tS, ad, bd, idS128, kk > 0 ? 1u : 0u);
+              const uint64_t off = uint64_t(((kk / 4) * C::kRowBox + (kk % 4) * 32) >> 4);
+              mma_ss(tS, qd0 + off, kd0 + off, idS128, kk > 0 ? 1u : 0u);
             }
             tc_commit(&empty_k[n % C::kSK]);
           } else {       // S = Q . kc_g^T, N = 32
-            const uint32_t st = smem_u32(sm + C::kOffRing2 + int(g % C::kS2) * C::kSlot2);
+            const uint64_t cd0 =
+                umma_desc_sw128(smem_u32(sm + C::kOffRing2 + int(g % C::kS2) * C::kSlot2), 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
-              const int bx = kk / 4, ko = (kk % 4) * 32;
-              const uint64_t ad = umma_desc_sw128(q_base + bx * C::kRowBox + ko, 16, 1024);
-              const uint64_t bd = umma_desc_sw128(st + bx * (kGroup * 128) + ko, 16, 1024);
-              mma_ss(tS, ad, bd, idS32, kk > 0 ? 1u : 0u);
+              const uint64_t aoff = uint64_t(((kk / 4) * C::kRowBox + (kk % 4) * 32) >> 4);
+              const uint64_t boff = uint64_t(((kk / 4) * (kGroup * 128) + (kk % 4) * 32) >> 4);
+              mma_ss(tS, qd0 + aoff, cd0 + boff, idS32, kk > 0 ? 1u : 0u);
             }
           }
           PASA_TRACE_MARK(28, n);
@@ -421,26 +424,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           tc_fence_after();
           const uint32_t tP = tmem + C::kColP + 64u * uint32_t(m & 1);
           if (m < nP) {  // K = 128: the two key blocks of the step
-            const uint32_t vst = smem_u32(sm + C::kOffV + int(m % C::kSV) * C::kPairBytes);
+            const uint64_t vd0 =
+                umma_desc_sw128(smem_u32(sm + C::kOffV + int(m % C::kSV) * C::kPairBytes), C::kRowBox, 1024);
 #pragma unroll
-            for (int kk = 0; kk < 2 * kBlock / 16; ++kk) {
-              const uint64_t bd = umma_desc_sw128(vst + kk * 2048, C::kRowBox, 1024);
-              mma_ts(tmem + C::kColO, tP + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < 2 * kBlock / 16; ++kk)
+              mma_ts(tmem + C::kColO, tP + kk * 8, vd0 + uint64_t((kk * 2048) >> 4), idPV,
+                     (m > 0 || kk > 0) ? 1u : 0u);
             tc_commit(&empty_v[m % C::kSV]);
           } else {
             const uint32_t st = smem_u32(sm + C::kOffRing2 + int(g % C::kS2) * C::kSlot2);
             const uint32_t tU = tmem + C::kColS0 + 128u * uint32_t((m + 1) & 1) + C::kColU;
+            const uint64_t vcd0 = umma_desc_sw128(st + C::kCBytes, C::kCBytes / C::kBoxes, 1024);
+            const uint64_t hd0 = umma_desc_sw128(st + 2 * C::kCBytes, C::kHBytes / C::kBoxes, 1024);
 #pragma unroll
-            for (int kk = 0; kk < kGroup / 16; ++kk) {
-              const uint64_t bd = umma_desc_sw128(st + C::kCBytes + kk * 2048, C::kCBytes / C::kBoxes, 1024);
-              mma_ts(tmem + C::kColO, tP + kk * 8, bd, idPV, 1u);
-            }
+            for (int kk = 0; kk < kGroup / 16; ++kk)
+              mma_ts(tmem + C::kColO, tP + kk * 8, vcd0 + uint64_t((kk * 2048) >> 4), idPV, 1u);
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint64_t bd = umma_desc_sw128(st + 2 * C::kCBytes + kk * 2048, C::kHBytes / C::kBoxes, 1024);
-              mma_ts(tmem + C::kColO, tU + kk * 8, bd, idPV, 1u);
-            }
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_ts(tmem + C::kColO, tU + kk * 8, hd0 + uint64_t((kk * 2048) >> 4), idPV, 1u);
             tc_commit(&empty2[g % C::kS2]);
           }
           tc_commit(&o_done[m & 1]);
