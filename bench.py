@@ -127,9 +127,11 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle (numpy restatement of the reference) on a sample
 # ---------------------------------------------------------------------------
-def cpu_baseline(w, seed=0, qblocks=16, budget_s=30.0):
-    """Time the oracle on one head: full block statistics and selection, and
-    attention for ``qblocks`` query blocks; extrapolate to the whole call."""
+def cpu_baseline(w, seed=0, target_s=12.0):
+    """Time the oracle on one head: full block statistics and selection, then
+    attention for as many query blocks (spread over the head) as fill about
+    ``target_s`` seconds, measured after a 4-block probe; extrapolate to the
+    whole call (all query blocks of all heads)."""
     import numpy as np
     import torch
 
@@ -150,11 +152,17 @@ def cpu_baseline(w, seed=0, qblocks=16, budget_s=30.0):
     hg = O.group_mean(hc, 32, dt)
     idx, _ = O.select_blocks(qc, kc, hn, w.D ** -0.5, w.NS, dt)
     t_stats = time.perf_counter() - t0
-    nq = min(qblocks, w.NT)
-    sel = np.linspace(0, w.NT - 1, nq).astype(np.int64)
-    t1 = time.perf_counter()
-    O.attention(qf, kf, vf, kc, vc, hg, idx, w.D ** -0.5, w.T, dtype=dt, qblocks=sel)
-    t_attn = time.perf_counter() - t1
+
+    def attn(nq):
+        sel = np.linspace(0, w.NT - 1, nq).astype(np.int64)
+        t1 = time.perf_counter()
+        O.attention(qf, kf, vf, kc, vc, hg, idx, w.D ** -0.5, w.T, dtype=dt, qblocks=sel)
+        return time.perf_counter() - t1
+
+    probe = min(4, w.NT)
+    per_block = attn(probe) / probe
+    nq = int(max(probe, min(w.NT, (target_s - t_stats) / max(per_block, 1e-6))))
+    t_attn = attn(nq)
     per_head = t_stats + t_attn * (w.NT / nq)
     total_s = per_head * w.heads
     value = w.exact_flops() / total_s / 1e12
@@ -207,7 +215,7 @@ def run_reference(args):
     vals = []
     last = None
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(w, seed=0, qblocks=4 if i < args.warmup else 8)
+        r = cpu_baseline(w, seed=0, target_s=3.0 if i < args.warmup else 12.0)
         if i >= args.warmup:
             vals.append(r["value"])
             last = r
