@@ -59,25 +59,30 @@ __device__ __forceinline__ void load_block(__nv_bfloat16* stage, const __nv_bflo
   }
 }
 
-// halving-tree column sum in bf16 (each partial sum rounded), as prep.cu;
-// the roundings alternate between the packed conversion and the integer pipe
+// bf16 addition of two pairs, rounded to nearest even: for bf16 inputs the
+// same value as adding in fp32 and rounding the sum to bf16 (an exact sum of
+// two 8-bit significands that differ by up to 15 binary places fits fp32;
+// beyond that the smaller one lies below half a bf16 step, so the fp32
+// rounding cannot create a tie).
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Halving-tree column sums in bf16 (each partial sum rounded, as prep.cu)
+// of columns c and c + 1 at once; returns them packed (c in the low half).
 template <int D>
-__device__ __forceinline__ float tree_sum(const __nv_bfloat16* tile, int c) {
+__device__ __forceinline__ uint32_t tree_sum2(const __nv_bfloat16* tile, int c) {
   using C = Cfg<D>;
-  float x[kBlock];
+  uint32_t x[kBlock];
 #pragma unroll
-  for (int r = 0; r < kBlock; ++r) x[r] = __bfloat162float(tile[r * C::kRS + c]);
+  for (int r = 0; r < kBlock; ++r) x[r] = *reinterpret_cast<const uint32_t*>(tile + r * C::kRS + c);
 #pragma unroll
-  for (int n = kBlock; n > 2; n >>= 1) {  // every level but the last has an even count: packed roundings
+  for (int n = kBlock; n > 1; n >>= 1)
 #pragma unroll
-    for (int r = 0; r < n / 2; r += 2) {
-      float a = x[r] + x[r + n / 2], b = x[r + 1] + x[r + 1 + n / 2];
-      round_bf16_pair(a, b);
-      x[r] = a;
-      x[r + 1] = b;
-    }
-  }
-  return round_bf16_int(x[0] + x[1]);
+    for (int r = 0; r < n / 2; ++r) x[r] = add_bf16x2(x[r], x[r + n / 2]);
+  return x[0];
 }
 
 template <int D>
@@ -138,18 +143,21 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
     const int64_t t0 = j * kBlock;
     const float len = float((T_len - t0 < kBlock) ? (T_len - t0) : int64_t(kBlock));  // BLOCK_SIZE (:91)
 
-    for (int task = tid; task < 3 * D; task += kThreads) {
-      const int which = task / D, c = task % D;
+    for (int task = tid; task < 3 * (D / 2); task += kThreads) {  // two columns per task
+      const int which = task / (D / 2), c = 2 * (task % (D / 2));
+      const uint32_t sum2 = tree_sum2<D>(which == 0 ? sq : (which == 1 ? sk : sv), c);
+      const float s0 = __uint_as_float(sum2 << 16), s1 = __uint_as_float(sum2 & 0xFFFF0000u);
       if (which == 0) {
-        qc_row[c] = __float2bfloat16_rn(__fdiv_rn(tree_sum<D>(sq, c), len));
+        *reinterpret_cast<uint32_t*>(qc_row + c) = pack_bf16x2(__fdiv_rn(s0, len), __fdiv_rn(s1, len));
       } else if (which == 1) {
-        const float m = __fdiv_rn(tree_sum<D>(sk, c), len);
-        kc_f[c] = m;
-        kc_row[c] = __float2bfloat16_rn(m);
+        const float m0 = __fdiv_rn(s0, len), m1 = __fdiv_rn(s1, len);
+        kc_f[c] = m0;
+        kc_f[c + 1] = m1;
+        *reinterpret_cast<uint32_t*>(kc_row + c) = pack_bf16x2(m0, m1);
       } else {
-        const float s = tree_sum<D>(sv, c);
-        vc_f[c] = s;
-        vc_row[c] = __float2bfloat16_rn(s);
+        vc_f[c] = s0;
+        vc_f[c + 1] = s1;
+        *reinterpret_cast<uint32_t*>(vc_row + c) = sum2;
       }
     }
 
