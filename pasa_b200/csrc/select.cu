@@ -281,34 +281,49 @@ __global__ void __launch_bounds__(kThreadsTC, 1) select_tc_kernel(
   }
 
   const int gq = lane >> 2, tq = lane & 3;
+  // the kc rows of the next chunk are loaded into registers while the current
+  // chunk is scored, so the L2 latency of the staging overlaps the MMAs
+  constexpr int kLoads = kKeyChunk * kVec / kThreadsTC;
+  static_assert(kKeyChunk * kVec % kThreadsTC == 0, "staging split");
+  uint4 pre[kLoads];
+  float hpre = 0.f, npre = 0.f;  // h_norm and noise of key block j0 + tid (tid < kKeyChunk)
+  auto fetch = [&](int64_t j0) {
+#pragma unroll
+    for (int it = 0; it < kLoads; ++it) {
+      const int x = tid + it * kThreadsTC, jj = x / kVec, c = x % kVec;
+      pre[it] = (j0 + jj < NT) ? reinterpret_cast<const uint4*>(kc + (bh * NTP + j0 + jj) * D)[c]
+                               : make_uint4(0, 0, 0, 0);
+    }
+    if (use_cov_bias && tid < kKeyChunk && j0 + tid < NT) {
+      hpre = h_norm[bh * NT + j0 + tid];
+      if (noise) npre = noise[bh * NT + j0 + tid];
+    }
+  };
+  fetch(0);
   for (int64_t j0 = 0; j0 < NT; j0 += kKeyChunk) {
     __syncthreads();
-    // kc * scale rounded to bf16 (:365), staged for the MMA
-    for (int x = tid; x < kKeyChunk * kVec; x += kThreadsTC) {
-      const int jj = x / kVec, c = x % kVec;
-      uint4 out = make_uint4(0, 0, 0, 0);
-      if (j0 + jj < NT) {
-        const uint4 in = reinterpret_cast<const uint4*>(kc + (bh * NTP + j0 + jj) * D)[c];
-        const uint32_t w[4] = {in.x, in.y, in.z, in.w};
-        uint32_t o[4];
+    // kc * scale rounded to bf16 (:365), staged for the MMA (rows >= NT: zero)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
-          o[e] = pack_bf16x2(f.x * scale32, f.y * scale32);
-        }
-        out = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int it = 0; it < kLoads; ++it) {
+      const int x = tid + it * kThreadsTC, jj = x / kVec, c = x % kVec;
+      const uint32_t w[4] = {pre[it].x, pre[it].y, pre[it].z, pre[it].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+        o[e] = pack_bf16x2(f.x * scale32, f.y * scale32);
       }
-      *reinterpret_cast<uint4*>(ks + jj * RS + c * 8) = out;
+      *reinterpret_cast<uint4*>(ks + jj * RS + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
     if (tid < kKeyChunk) {
-      const int64_t j = j0 + tid;
       float b = 0.f;
-      if (use_cov_bias && j < NT) {
-        b = logf(h_norm[bh * NT + j] + 1e-6f);  // :368
-        if (noise) b = b + noise[bh * NT + j];  // :370
+      if (use_cov_bias && j0 + tid < NT) {
+        b = logf(hpre + 1e-6f);  // :368
+        if (noise) b = b + npre;  // :370
       }
       bias[tid] = b;
     }
+    if (j0 + kKeyChunk < NT) fetch(j0 + kKeyChunk);
     __syncthreads();
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const int kb = warp * 8;  // this warp's 8 key blocks within the chunk
