@@ -109,11 +109,55 @@ __device__ __forceinline__ void row_topk(const uint32_t* rk, int64_t NT, int64_t
       base += __popc(b);
     }
     __syncwarp();
-    for (int64_t e = lane; e < NS; e += 32) {
-      const uint64_t me = cl[e];
-      int64_t rank = 0;
-      for (int64_t f = 0; f < NS; ++f) rank += (cl[f] > me) ? 1 : 0;
-      out[rank] = int32_t(0xFFFFFFFFu - uint32_t(me & 0xFFFFFFFFu));
+    if (NS <= 128) {
+      // bitonic sort (descending) of the composites, 4 per lane at positions
+      // 4 * lane + u; padding 0 sorts last (every composite is > 0: its low
+      // word is 0xFFFFFFFF - j with j < 2^24)
+      uint64_t v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = 4 * lane + u;
+        v[u] = (i < NS) ? cl[i] : 0ull;
+      }
+#pragma unroll
+      for (int k = 2; k <= 128; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          if (j >= 4) {  // partner in lane ^ (j / 4), same slot
+            const int lm = j >> 2;
+            const bool lower = (lane & lm) == 0;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const uint64_t o = __shfl_xor_sync(0xffffffffu, v[u], lm);
+              const bool desc = ((4 * lane + u) & k) == 0;
+              v[u] = (lower == desc) ? (v[u] > o ? v[u] : o) : (v[u] < o ? v[u] : o);
+            }
+          } else {       // partner in this lane: slot u ^ j
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if ((u & j) != 0) continue;
+              const int w = u | j;
+              const bool desc = ((4 * lane + u) & k) == 0;
+              const uint64_t a = v[u], b = v[w];
+              const bool swap = desc ? (a < b) : (a > b);
+              v[u] = swap ? b : a;
+              v[w] = swap ? a : b;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = 4 * lane + u;
+        if (i < NS) out[i] = int32_t(0xFFFFFFFFu - uint32_t(v[u] & 0xFFFFFFFFu));
+      }
+    } else {
+      for (int64_t e = lane; e < NS; e += 32) {
+        const uint64_t me = cl[e];
+        int64_t rank = 0;
+        for (int64_t f = 0; f < NS; ++f) rank += (cl[f] > me) ? 1 : 0;
+        out[rank] = int32_t(0xFFFFFFFFu - uint32_t(me & 0xFFFFFFFFu));
+      }
     }
   } else {
     for (int64_t j = lane; j < NT; j += 32) {
