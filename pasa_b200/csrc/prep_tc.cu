@@ -115,6 +115,13 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
 
   const int64_t j_first = g * kGroup;
   const int nvalid = int((NT - j_first) < kGroup ? (NT - j_first) : kGroup);  // blocks of this group < NT
+  // h_norm of block b from the per-warp partial sums, double-buffered by b's
+  // parity; thread 0 finishes it after the next barrier
+  auto finish_norm = [&](int b) {
+    float tot = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) tot += red[(b & 1) * (kThreads / 32) + w];
+    h_norm[bh * NT + j_first + b] = __fsqrt_rn(tot);  // :287
+  };
   if (nvalid > 0) load_block<D>(stages, qh, kh, vh, j_first * kBlock, T_len);
   cp_async_commit();
 
@@ -136,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
+    if (tid == 0 && jj > 0) finish_norm(jj - 1);  // every warp wrote its part of block jj-1 before this barrier
     const __nv_bfloat16* st = stages + (jj & 1) * C::kStage;
     const __nv_bfloat16* sq = st;
     const __nv_bfloat16* sk = st + C::kTile;
@@ -208,16 +216,15 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
         }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) nsq += __shfl_xor_sync(0xffffffffu, nsq, off);
-    if (lane == 0) red[warp] = nsq;
-    __syncthreads();
-    if (tid == 0) {
-      float tot = 0.f;
-      for (int w = 0; w < kThreads / 32; ++w) tot += red[w];
-      h_norm[bh * NT + j] = __fsqrt_rn(tot);  // :287
-    }
-    // the stage just read is refilled two iterations later, after this barrier
+    if (lane == 0) red[(jj & 1) * (kThreads / 32) + warp] = nsq;
+    // No barrier here.  The next block's first barrier orders red and the
+    // next writes of kc_f / vc_f after this epilogue.  This block's stage was
+    // last read (tree sums, MMA fragments) before the kc_f / vc_f barrier
+    // above, so the next block's prefetch may refill it.
   }
   cp_async_wait<0>();
+  __syncthreads();
+  if (tid == 0 && nvalid > 0) finish_norm(nvalid - 1);
 
   __nv_bfloat16* hg = h_group + ((bh * NG + g) * D) * D;
 #pragma unroll
