@@ -201,19 +201,29 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
     }
     __syncthreads();  // kc_f / vc_f written above
 
-    float nsq = 0.f;
+    // elements e, e+1 of a fragment are columns b, b+1 of one row: packed
+    // fp32 pair instructions (per-lane results as the scalar forms)
+    float2 nsq2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int mi = 0; mi < C::MI; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < C::NI; ++ni)
+      for (int ni = 0; ni < C::NI; ++ni) {
+        const int b = bn + ni * 8 + 2 * tq;
+        const float2 vb = make_float2(vc_f[b], vc_f[b + 1]);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int a = am + mi * 16 + gq + ((e >= 2) ? 8 : 0);
-          const int b = bn + ni * 8 + 2 * tq + (e & 1);
-          const float hc = fmaf(-kc_f[a], vc_f[b], acc[mi][ni][e]);  // :106-107
-          nsq = fmaf(hc, hc, nsq);                                     // :110
-          gsum[mi][ni][e] += round_bf16_int(hc);                      // hc stored in v dtype (:125)
+        for (int e = 0; e < 4; e += 2) {
+          const float nk = -kc_f[am + mi * 16 + gq + ((e >= 2) ? 8 : 0)];
+          const float2 hc = __ffma2_rn(make_float2(nk, nk), vb,
+                                       make_float2(acc[mi][ni][e], acc[mi][ni][e + 1]));  // :106-107
+          nsq2 = __ffma2_rn(hc, hc, nsq2);                                                // :110
+          // hc stored in v dtype (:125): both roundings in one conversion
+          const float2 hr = __bfloat1622float2(__floats2bfloat162_rn(hc.x, hc.y));
+          const float2 gs = __fadd2_rn(make_float2(gsum[mi][ni][e], gsum[mi][ni][e + 1]), hr);
+          gsum[mi][ni][e] = gs.x;
+          gsum[mi][ni][e + 1] = gs.y;
         }
+      }
+    float nsq = nsq2.x + nsq2.y;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) nsq += __shfl_xor_sync(0xffffffffu, nsq, off);
     if (lane == 0) red[(jj & 1) * (kThreads / 32) + warp] = nsq;
