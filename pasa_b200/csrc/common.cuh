@@ -40,21 +40,6 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ void store(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
 };
 
-// fp32 -> bf16 -> fp32 with round-to-nearest-even, on the integer pipe: add
-// half an ulp of bf16 (0x7FFF, plus the kept bit's parity for ties) to the
-// bit pattern and clear the low 16 bits.  Equals the conversion instruction
-// for every finite input (subnormals included); inputs here are finite sums.
-__device__ __forceinline__ float round_bf16_int(float x) {
-  const uint32_t b = __float_as_uint(x);
-  return __uint_as_float((b + 0x7FFFu + ((b >> 16) & 1u)) & 0xFFFF0000u);
-}
-// Two roundings with one packed conversion (cvt.rn.bf16x2.f32).
-__device__ __forceinline__ void round_bf16_pair(float& lo, float& hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  lo = __low2float(h);
-  hi = __high2float(h);
-}
-
 // 2^x with the hardware approximation (ex2.approx.f32), the instruction the
 // reference's tl.math.exp2 lowers to.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -143,30 +128,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// try_wait with an explicit suspend-time hint (ns): the thread sleeps in
-// hardware until the phase completes or the hint elapses, instead of
-// re-issuing the probe and taking issue slots from its sub-partition.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
-  return ok != 0;
-}
-
-// Non-blocking probe of a phase (mbarrier.test_wait).
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-  return ok != 0;
-}
-
 // SM clock cycles (cheap to read; compared only within one thread).
 __device__ __forceinline__ uint64_t sm_cycles() { return clock64(); }
 
@@ -181,20 +142,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = sm_cycles();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (sm_cycles() - t0 > limit) return false;
-  }
-}
-
-// Bounded wait with a sleep between probes, for helper threads (TMA
-// producer, MMA issuers) that wait long and often: a probe loop would take
-// issue slots from the softmax warps sharing the thread's sub-partition.
-__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
-                                                  uint64_t limit = kWaitLimitCycles) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = sm_cycles();
-  for (;;) {
-    __nanosleep(sleep_ns);
     if (mbar_try_wait(bar, parity)) return true;
     if (sm_cycles() - t0 > limit) return false;
   }
@@ -319,40 +266,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
-      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};"
-               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]) : "memory");
-}
-
-// Whole-array TMEM load / store of N consecutive columns (load: 8, 16, 32;
-// store: 4, 8, 16, 32).
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
-  static_assert(N == 8 || N == 16 || N == 32, "tmem_ld width");
-  if constexpr (N == 32) tmem_ld32(taddr, r);
-  else if constexpr (N == 16) tmem_ld16(taddr, r);
-  else tmem_ld8(taddr, r);
-}
-template <int N>
-__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) {
-  static_assert(N == 4 || N == 8 || N == 16 || N == 32, "tmem_st width");
-  if constexpr (N == 32) tmem_st32(taddr, r);
-  else if constexpr (N == 16) tmem_st16(taddr, r);
-  else if constexpr (N == 8) tmem_st8(taddr, r);
-  else tmem_st4(taddr, r);
-}
-
 // Named barrier over `nthreads` threads (multiple of 32); id 0 is __syncthreads.
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
@@ -369,7 +282,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Maximum of 32 / 16 fp32 values held as raw bits (shallow tree of 3-input max).
+// Maximum of 32 fp32 values held as raw bits (shallow tree of 3-input max).
 __device__ __forceinline__ float max_tree32(const uint32_t (&v)[32]) {
   float m[12];
 #pragma unroll
@@ -381,29 +294,7 @@ __device__ __forceinline__ float max_tree32(const uint32_t (&v)[32]) {
   const float c = fmax3(m[6], m[7], m[8]), d = fmax3(m[9], m[10], m[11]);
   return fmaxf(fmax3(a, b, c), d);
 }
-__device__ __forceinline__ float max_tree8(const uint32_t (&v)[8]) {
-  const float a = fmax3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-  const float b = fmax3(__uint_as_float(v[3]), __uint_as_float(v[4]), __uint_as_float(v[5]));
-  return fmax3(a, b, fmaxf(__uint_as_float(v[6]), __uint_as_float(v[7])));
-}
-__device__ __forceinline__ float max_tree16(const uint32_t (&v)[16]) {
-  float m[6];
-#pragma unroll
-  for (int i = 0; i < 5; ++i)
-    m[i] = fmax3(__uint_as_float(v[3 * i]), __uint_as_float(v[3 * i + 1]), __uint_as_float(v[3 * i + 2]));
-  m[5] = __uint_as_float(v[15]);
-  return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi);
-
-template <int N>
-__device__ __forceinline__ float max_tree(const uint32_t (&v)[N]) {
-  static_assert(N == 8 || N == 16 || N == 32, "max_tree width");
-  if constexpr (N == 32) return max_tree32(v);
-  else if constexpr (N == 16) return max_tree16(v);
-  else return max_tree8(v);
-}
 
 // p_c = 2^(s_c * scale + negm) for N (a multiple of 4) raw fp32 scores;
 // packs bf16 pairs into pk and returns the fp32 sum of the p_c.  The
