@@ -562,29 +562,43 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           if (m_applied != -INFINITY) l1 *= fast_exp2(m_applied - m_used);
           m_applied = m_used;
         }
+        // pass 2: probabilities of both blocks into registers (block 0: keys
+        // 0-63 -> P columns 0-31, block 1 -> columns 32-63).  The S buffer is
+        // free after the last load, before any wait, and the exponentials run
+        // while the P.V of step n-2 still reads this set's P region.
+        const float negm = -m_used;
+        uint32_t p0a[16], p0b[16], p1a[16], p1b[16];
+        if (!act0 && !act1) free_s();
+        if (act0) {
+          load_block(0, last0);
+          if (!act1) free_s();
+          l1 += exp2_pack<32>(sa, sm_scale, negm, p0a);
+          l1 += exp2_pack<32>(sb, sm_scale, negm, p0b);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) { p0a[c] = 0u; p0b[c] = 0u; }
+        }
+        if (act1) {  // block 1 in two halves: block 0's P is held meanwhile
+          tmem_ld32(tS + 64, sa);
+          tmem_wait_ld();
+          if (last1) mask_tail<32>(sa, int(last_len));
+          l1 += exp2_pack<32>(sa, sm_scale, negm, p1a);
+          tmem_ld32(tS + 96, sb);
+          tmem_wait_ld();
+          free_s();
+          if (last1) mask_tail<32>(sb, int(last_len) - 32);
+          l1 += exp2_pack<32>(sb, sm_scale, negm, p1b);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) { p1a[c] = 0u; p1b[c] = 0u; }
+        }
         // this set's P region was last read by the P.V of step n-2
         if (n >= 2) { wait_bar(&o_done[n & 1], (n - 2) >> 1); tc_fence_after(); }
         if (warp == 3 && lane == 0) PASA_TRACE_MARK(26, n);
-        // pass 2: probabilities, block by block, straight into the P region
-        // (block 0: keys 0-63 -> columns 0-31, block 1 -> columns 32-63)
-        const float negm = -m_used;
-        uint32_t pa[16], pb[16];
-        if (!act0 && !act1) free_s();
-#pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          const bool act = blk == 0 ? act0 : act1;
-          if (act) {
-            load_block(blk, blk == 0 ? last0 : last1);
-            if (blk == 1 || !act1) free_s();
-            l1 += exp2_pack<32>(sa, sm_scale, negm, pa);
-            l1 += exp2_pack<32>(sb, sm_scale, negm, pb);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 16; ++c) { pa[c] = 0u; pb[c] = 0u; }
-          }
-          tmem_st16(tP + 32 * blk, pa);
-          tmem_st16(tP + 32 * blk + 16, pb);
-        }
+        tmem_st16(tP, p0a);
+        tmem_st16(tP + 16, p0b);
+        tmem_st16(tP + 32, p1a);
+        tmem_st16(tP + 48, p1b);
         if (warp == 3 && lane == 0) PASA_TRACE_MARK(27, n);
         tmem_wait_st();
       } else {
@@ -645,12 +659,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // the other set's S buffer; at the first group that buffer held the
         // full-width scores of step n-1, which that set loaded before it
         // handed over the maxima of step n-1 (advance_max above).
-        if (n >= 2) { wait_bar(&o_done[n & 1], (n - 2) >> 1); tc_fence_after(); }
-        tmem_st16(tP, pk);
-        // U = bf16(w q) over all D columns, from this row of Q in shared memory
+        // U = bf16(w q) over all D columns, from this row of Q in shared
+        // memory, built before the wait so that it overlaps the P.V of n-2
+        uint32_t u[C::kBoxes][32];
 #pragma unroll
         for (int bx = 0; bx < C::kBoxes; ++bx) {
-          uint32_t u[32];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint4 qv = *reinterpret_cast<const uint4*>(sm + C::kOffQ + bx * C::kRowBox + r * 128 +
@@ -659,11 +672,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
               const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[x]));
-              u[c * 4 + x] = pack_bf16x2(qf.x * w, qf.y * w);
+              u[bx][c * 4 + x] = pack_bf16x2(qf.x * w, qf.y * w);
             }
           }
-          tmem_st32(tUo + bx * 32, u);
         }
+        if (n >= 2) { wait_bar(&o_done[n & 1], (n - 2) >> 1); tc_fence_after(); }
+        tmem_st16(tP, pk);
+#pragma unroll
+        for (int bx = 0; bx < C::kBoxes; ++bx) tmem_st32(tUo + bx * 32, u[bx]);
         tmem_wait_st();
       }
       // hand P (and U) of step n to the P.V issuer
