@@ -20,8 +20,11 @@
 //     query blocks) walks the 32-block groups with each half's own selection
 //     bits, one group per step.
 //   * Q stays in shared memory as the A operand of every score MMA; K and V
-//     of a step have separate rings (K runs three steps ahead, V two), and
-//     phase 2's kc/vc/H ring is aliased on the same memory.
+//     of a step have separate rings (K runs three steps ahead, V two).
+//     Phase 2's rings are aliased on the same memory: kc rows (five groups,
+//     freed by the score MMAs) and vc rows + H (three groups, freed by the
+//     correction MMAs), so the score MMAs of later groups never wait for an
+//     earlier group's correction to free a slot.
 //   * TMEM (512 columns): O (128, fp32), two P regions (64 each, bf16) and
 //     two S buffers (128 each).  Step n uses S buffer n & 1 and P region n & 1.
 //   * warp 0: TMA producer; warp 1: TMEM owner and score-MMA issuer; warp 2:
@@ -74,8 +77,15 @@ struct Cfg {
   static constexpr int kSK = 3;                         // K ring slots
   static constexpr int kSV = 2;                         // V ring slots
   static constexpr int kKVRegion = (kSK + kSV) * kPairBytes;
-  static constexpr int kSlot2 = 2 * kCBytes + kHBytes;  // phase-2 slot: kc rows, vc rows, H of one group
-  static constexpr int kS2 = kKVRegion / kSlot2;
+  // Phase 2 has two rings, aliased on the K and V rings: kc rows (read by
+  // the score MMAs) and vc rows + H (read by the P.V issuer).  Each is
+  // released by its own reader, so the next groups' kc need not wait for
+  // the correction MMAs of an earlier group to free a shared slot.
+  static constexpr int kSlotH = kCBytes + kHBytes;      // vc rows and H of one group
+  static constexpr int kSH = 3;                         // vc/H ring slots
+  static constexpr int kSCFit = (kKVRegion - kSH * kSlotH) / kCBytes;
+  static constexpr int kSC = kSCFit < 8 ? kSCFit : 8;   // kc ring slots
+  static constexpr int kLagH = 2;                       // kc loads run this many groups ahead of vc/H
   // TMEM columns
   static constexpr uint32_t kColO = 0;
   static constexpr uint32_t kColP = 128;                // P region b at kColP + 64 b
@@ -86,16 +96,17 @@ struct Cfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;                      // K ring, then V ring
   static constexpr int kOffV = kOffK + kSK * kPairBytes;
-  static constexpr int kOffRing2 = kOffK;                            // aliased on the K and V rings
+  static constexpr int kOffRingC = kOffK;                            // aliased on the K and V rings
+  static constexpr int kOffRingH = kOffRingC + kSC * kCBytes;
   static constexpr int kOffUnion = kOffK + kKVRegion;                // u16 [kMaxNT]
   static constexpr int kOffMask = kOffUnion + kMaxNT * 2;            // u32 [2][kMaxNG]
   static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][2 sets][128]
   static constexpr int kOffHand = kOffXch + 2 * 2 * kRowsPerTile * 4;  // f32 [2 sets][m_used, m_true][128]
   static constexpr int kOffBar = kOffHand + 2 * 2 * kRowsPerTile * 4;
-  static constexpr int kNumBars = 2 * kSK + 2 * kSV + 2 * kS2 + 1 + 2 + 2 + 2 + 2;
+  static constexpr int kNumBars = 2 * kSK + 2 * kSV + 2 * kSC + 2 * kSH + 1 + 2 + 2 + 2 + 2;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
-  static_assert(kS2 >= 2, "phase-2 ring too small");
+  static_assert(kSC >= kSH + kLagH && kOffRingH + kSH * kSlotH <= kOffK + kKVRegion, "phase-2 rings");
   static_assert(kColS0 + 2 * 128 <= kTmemCols, "TMEM budget");
   static_assert(kColO + D <= kColP, "O must fit below P");
   static_assert(kColU + D / 2 <= 128, "U must fit in the S buffer");
@@ -169,9 +180,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* empty_k = full_k + C::kSK;
   uint64_t* full_v = empty_k + C::kSK;
   uint64_t* empty_v = full_v + C::kSV;
-  uint64_t* full2 = empty_v + C::kSV;
-  uint64_t* empty2 = full2 + C::kS2;
-  uint64_t* q_full = empty2 + C::kS2;
+  uint64_t* full_c = empty_v + C::kSV;
+  uint64_t* empty_c = full_c + C::kSC;
+  uint64_t* full_h = empty_c + C::kSC;
+  uint64_t* empty_h = full_h + C::kSH;
+  uint64_t* q_full = empty_h + C::kSH;
   uint64_t* s_full = q_full + 1;   // [2] scores of S buffer b are in TMEM
   uint64_t* s_free = s_full + 2;   // [2] set b holds the scores of its step in registers
   uint64_t* p_ready = s_free + 2;  // [2] set b's P (and U) of its step are in TMEM
@@ -193,7 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   if (tid == 0) {
     for (int s = 0; s < C::kSK; ++s) { mbar_init(&full_k[s], 1); mbar_init(&empty_k[s], 1); }
     for (int s = 0; s < C::kSV; ++s) { mbar_init(&full_v[s], 1); mbar_init(&empty_v[s], 1); }
-    for (int s = 0; s < C::kS2; ++s) { mbar_init(&full2[s], 1); mbar_init(&empty2[s], 1); }
+    for (int s = 0; s < C::kSC; ++s) { mbar_init(&full_c[s], 1); mbar_init(&empty_c[s], 1); }
+    for (int s = 0; s < C::kSH; ++s) { mbar_init(&full_h[s], 1); mbar_init(&empty_h[s], 1); }
     mbar_init(q_full, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1); mbar_init(&s_free[b], kSetWarps);
@@ -336,26 +350,40 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         if (!mbar_wait_bounded(&empty_k[p % C::kSK], uint32_t((p / C::kSK) & 1), kPollLimit)) ok = false;
       for (int64_t p = (nP > C::kSV ? nP - C::kSV : 0); p < nP && ok; ++p)
         if (!mbar_wait_bounded(&empty_v[p % C::kSV], uint32_t((p / C::kSV) & 1), kPollLimit)) ok = false;
-      // Phase 2: kc, vc rows and H of every group through ring 2
-      int64_t issued2 = 0;
-      for (int64_t g = 0; g < NG2 && ok; ++g) {
-        const int s = int(g % C::kS2);
-        if (!mbar_wait_bounded(&empty2[s], uint32_t((g / C::kS2) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
-        PASA_TRACE_MARK(0, nP + g);
-        unsigned char* st = sm + C::kOffRing2 + s * C::kSlot2;
-        mbar_arrive_expect_tx(&full2[s], C::kSlot2);
-        for (int bx = 0; bx < C::kBoxes; ++bx) {
-          tma_load_3d(st + bx * (kGroup * 128), &maps.kc, &full2[s], bx * 64, int32_t(g * kGroup), int32_t(bh));
-          tma_load_3d(st + C::kCBytes + bx * (kGroup * 128), &maps.vc, &full2[s], bx * 64, int32_t(g * kGroup),
-                      int32_t(bh));
-          tma_load_3d(st + 2 * C::kCBytes + bx * (D * 128), &maps.h, &full2[s], bx * 64, 0, int32_t(bh * NG + g));
+      // Phase 2: kc rows of every group through ring C, vc rows and H
+      // through ring H, the kc loads kLagH groups ahead in issue order (ring
+      // C is released by the score MMAs, which run ahead of the P.V issuer)
+      int64_t issued_c = 0, issued_h = 0;
+      for (int64_t i = 0; i < NG2 + C::kLagH && ok; ++i) {
+        if (i < NG2) {
+          const int s = int(i % C::kSC);
+          if (!mbar_wait_bounded(&empty_c[s], uint32_t((i / C::kSC) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
+          PASA_TRACE_MARK(0, nP + i);
+          unsigned char* st = sm + C::kOffRingC + s * C::kCBytes;
+          mbar_arrive_expect_tx(&full_c[s], C::kCBytes);
+          for (int bx = 0; bx < C::kBoxes; ++bx)
+            tma_load_3d(st + bx * (kGroup * 128), &maps.kc, &full_c[s], bx * 64, int32_t(i * kGroup), int32_t(bh));
+          issued_c = i + 1;
         }
-        issued2 = g + 1;
+        const int64_t g = i - C::kLagH;
+        if (g >= 0) {
+          const int s = int(g % C::kSH);
+          if (!mbar_wait_bounded(&empty_h[s], uint32_t((g / C::kSH) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
+          unsigned char* st = sm + C::kOffRingH + s * C::kSlotH;
+          mbar_arrive_expect_tx(&full_h[s], C::kSlotH);
+          for (int bx = 0; bx < C::kBoxes; ++bx) {
+            tma_load_3d(st + bx * (kGroup * 128), &maps.vc, &full_h[s], bx * 64, int32_t(g * kGroup), int32_t(bh));
+            tma_load_3d(st + C::kCBytes + bx * (D * 128), &maps.h, &full_h[s], bx * 64, 0, int32_t(bh * NG + g));
+          }
+          issued_h = g + 1;
+        }
       }
       if (!ok) report(P.err);
       // drain: let this thread's last phase-2 copies land before the CTA can exit
-      for (int64_t g = (issued2 > C::kS2 ? issued2 - C::kS2 : 0); g < issued2; ++g)
-        mbar_wait_bounded(&full2[g % C::kS2], uint32_t((g / C::kS2) & 1), kPollLimit);
+      for (int64_t g = (issued_c > C::kSC ? issued_c - C::kSC : 0); g < issued_c; ++g)
+        mbar_wait_bounded(&full_c[g % C::kSC], uint32_t((g / C::kSC) & 1), kPollLimit);
+      for (int64_t g = (issued_h > C::kSH ? issued_h - C::kSH : 0); g < issued_h; ++g)
+        mbar_wait_bounded(&full_h[g % C::kSH], uint32_t((g / C::kSH) & 1), kPollLimit);
     }
   } else if (warp == 1 || warp == 2) {
     // ================= MMA issuers =================
@@ -384,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           const int64_t g = n - nP;  // phase-2 group, if any
           const bool landed = (n < nP)
               ? mbar_wait_bounded(&full_k[n % C::kSK], uint32_t((n / C::kSK) & 1), kPollLimit)
-              : mbar_wait_bounded(&full2[g % C::kS2], uint32_t((g / C::kS2) & 1), kPollLimit);
+              : mbar_wait_bounded(&full_c[g % C::kSC], uint32_t((g / C::kSC) & 1), kPollLimit);
           if (!landed) { ok = false; break; }
           PASA_TRACE_MARK(1, n);
           tc_fence_after();
@@ -400,13 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             tc_commit(&empty_k[n % C::kSK]);
           } else {       // S = Q . kc_g^T, N = 32
             const uint64_t cd0 =
-                umma_desc_sw128(smem_u32(sm + C::kOffRing2 + int(g % C::kS2) * C::kSlot2), 16, 1024);
+                umma_desc_sw128(smem_u32(sm + C::kOffRingC + int(g % C::kSC) * C::kCBytes), 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint64_t aoff = uint64_t(((kk / 4) * C::kRowBox + (kk % 4) * 32) >> 4);
               const uint64_t boff = uint64_t(((kk / 4) * (kGroup * 128) + (kk % 4) * 32) >> 4);
               mma_ss(tS, qd0 + aoff, cd0 + boff, idS32, kk > 0 ? 1u : 0u);
             }
+            tc_commit(&empty_c[g % C::kSC]);
           }
           PASA_TRACE_MARK(28, n);
           tc_commit(&s_full[n & 1]);
@@ -418,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           const int64_t g = m - nP;
           const bool landed = (m < nP)
               ? mbar_wait_bounded(&full_v[m % C::kSV], uint32_t((m / C::kSV) & 1), kPollLimit)
-              : mbar_wait_bounded(&full2[g % C::kS2], uint32_t((g / C::kS2) & 1), kPollLimit);
+              : mbar_wait_bounded(&full_h[g % C::kSH], uint32_t((g / C::kSH) & 1), kPollLimit);
           if (!landed) { ok = false; break; }
           PASA_TRACE_MARK(2, m);
           tc_fence_after();
@@ -432,17 +461,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                      (m > 0 || kk > 0) ? 1u : 0u);
             tc_commit(&empty_v[m % C::kSV]);
           } else {
-            const uint32_t st = smem_u32(sm + C::kOffRing2 + int(g % C::kS2) * C::kSlot2);
+            const uint32_t st = smem_u32(sm + C::kOffRingH + int(g % C::kSH) * C::kSlotH);
             const uint32_t tU = tmem + C::kColS0 + 128u * uint32_t((m + 1) & 1) + C::kColU;
-            const uint64_t vcd0 = umma_desc_sw128(st + C::kCBytes, C::kCBytes / C::kBoxes, 1024);
-            const uint64_t hd0 = umma_desc_sw128(st + 2 * C::kCBytes, C::kHBytes / C::kBoxes, 1024);
+            const uint64_t vcd0 = umma_desc_sw128(st, C::kCBytes / C::kBoxes, 1024);
+            const uint64_t hd0 = umma_desc_sw128(st + C::kCBytes, C::kHBytes / C::kBoxes, 1024);
 #pragma unroll
             for (int kk = 0; kk < kGroup / 16; ++kk)
               mma_ts(tmem + C::kColO, tP + kk * 8, vcd0 + uint64_t((kk * 2048) >> 4), idPV, 1u);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk)
               mma_ts(tmem + C::kColO, tU + kk * 8, hd0 + uint64_t((kk * 2048) >> 4), idPV, 1u);
-            tc_commit(&empty2[g % C::kS2]);
+            tc_commit(&empty_h[g % C::kSH]);
           }
           tc_commit(&o_done[m & 1]);
           PASA_TRACE_MARK(29, m);
