@@ -41,8 +41,9 @@
 //     registers, so the score MMAs of step n+2 run during the softmax of n.
 //   * Phase 2: group scores are 32 columns; P_g sits in the step's P region
 //     and the first-order operand U = bf16(w_t q_t) (w_t = scale * sum of the
-//     group's probabilities) in the upper half of the other S buffer, and
-//     U.H_g is accumulated straight into O by the tensor core.
+//     group's probabilities) in the upper half of the step's own S buffer
+//     (the group score MMAs write only its first 32 columns), and U.H_g is
+//     accumulated straight into O by the tensor core.
 //   * softmax rescales O only when a row max grows by more than 2^8
 //     (exact either way: O and l share the stale max); the exact running max
 //     is tracked separately to reproduce g_l.
@@ -90,7 +91,7 @@ struct Cfg {
   static constexpr uint32_t kColO = 0;
   static constexpr uint32_t kColP = 128;                // P region b at kColP + 64 b
   static constexpr uint32_t kColS0 = 256;               // S buffer b at kColS0 + 128 b
-  static constexpr uint32_t kColU = 64;                 // phase 2: U of step n in S buffer (n + 1) & 1
+  static constexpr uint32_t kColU = 64;                 // phase 2: U of step n in S buffer n & 1
   static constexpr uint32_t kTmemCols = 512;
   // shared memory carve-up (offsets from a 1024-aligned base)
   static constexpr int kOffQ = 0;
@@ -462,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             tc_commit(&empty_v[m % C::kSV]);
           } else {
             const uint32_t st = smem_u32(sm + C::kOffRingH + int(g % C::kSH) * C::kSlotH);
-            const uint32_t tU = tmem + C::kColS0 + 128u * uint32_t((m + 1) & 1) + C::kColU;
+            const uint32_t tU = tmem + C::kColS0 + 128u * uint32_t(m & 1) + C::kColU;
             const uint64_t vcd0 = umma_desc_sw128(st, C::kCBytes / C::kBoxes, 1024);
             const uint64_t hd0 = umma_desc_sw128(st + C::kCBytes, C::kHBytes / C::kBoxes, 1024);
 #pragma unroll
@@ -495,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     const uint32_t lane_base = uint32_t(quad * 32) << 16;
     const uint32_t tS = tmem + lane_base + C::kColS0 + 128u * uint32_t(set);  // this set's S buffer
     const uint32_t tP = tmem + lane_base + C::kColP + 64u * uint32_t(set);    // this set's P region
-    const uint32_t tUo = tmem + lane_base + C::kColS0 + 128u * uint32_t(set ^ 1) + C::kColU;  // U (other buffer)
+    const uint32_t tU = tmem + lane_base + C::kColS0 + 128u * uint32_t(set) + C::kColU;  // U (phase 2)
     const float scale32 = P.scale;
     const float sm_scale = scale32 * kLog2e;
     const int64_t last_len = P.T - (NT - 1) * kBlock;
@@ -685,9 +686,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           for (int c = 0; c < kGroup / 2; ++c) pk[c] = 0u;
         }
         // P region and U slot were last read by the P.V of step n-2.  U goes to
-        // the other set's S buffer; at the first group that buffer held the
-        // full-width scores of step n-1, which that set loaded before it
-        // handed over the maxima of step n-1 (advance_max above).
+        // columns 64-127 of this set's own S buffer: the group score MMAs
+        // write only columns 0-31, and this set read its last full-width
+        // scores there at step n-2.  (The other set's buffer would not do: at
+        // the first group that set may still be reading the full-width
+        // scores of step n-1 for its probabilities.)
         // U = bf16(w q) over all D columns, from this row of Q in shared
         // memory, built before the wait so that it overlaps the P.V of n-2
         uint32_t u[C::kBoxes][32];
@@ -708,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         if (n >= 2) { wait_bar(&o_done[n & 1], (n - 2) >> 1); tc_fence_after(); }
         tmem_st16(tP, pk);
 #pragma unroll
-        for (int bx = 0; bx < C::kBoxes; ++bx) tmem_st32(tUo + bx * 32, u[bx]);
+        for (int bx = 0; bx < C::kBoxes; ++bx) tmem_st32(tU + bx * 32, u[bx]);
         tmem_wait_st();
       }
       // hand P (and U) of step n to the P.V issuer
