@@ -646,10 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           // columns of selected blocks or of blocks >= NT are masked (:228)
           const int jb0 = int(g) * kGroup;  // NT <= kMaxNT fits in int
           const int lim = int(NT) - jb0;
-          const uint32_t word = maskw[half * kMaxNG + g];
+          const uint32_t dead = maskw[half * kMaxNG + g] |
+                                (lim >= kGroup ? 0u : (lim <= 0 ? ~0u : ~((1u << lim) - 1u)));
 #pragma unroll
           for (int c = 0; c < kGroup; ++c)
-            if (c >= lim || ((word >> c) & 1u)) sv[c] = __float_as_uint(-INFINITY);
+            if ((dead >> c) & 1u) sv[c] = __float_as_uint(-INFINITY);
           float mx = max_tree32(sv);
           mx = (mx == -INFINITY) ? mx : mx * sm_scale;
           float m_prev = m_used;
@@ -660,23 +661,29 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           if (m_applied != m_used) { l1 *= fast_exp2(m_applied - m_used); m_applied = m_used; }
           float p[kGroup];
           const float negm = -m_used;
-#pragma unroll
-          for (int c = 0; c < kGroup; ++c) p[c] = exp2_ftz(fmaf(__uint_as_float(sv[c]), sm_scale, negm));
-          float psum, wsum;
+          float2 acc = make_float2(0.f, 0.f);  // even / odd column sums
           {
-            float a0 = 0.f, a1 = 0.f, extra = 0.f;
-            // bit of the ragged last block's column, if it is in this group
-            // (a bit test, not an index: p[] must stay in registers)
-            const uint32_t lastbit = (lim >= 1 && lim <= kGroup) ? (1u << (lim - 1)) : 0u;
+            const float2 sc2 = make_float2(sm_scale, sm_scale), nm2 = make_float2(negm, negm);
 #pragma unroll
             for (int c = 0; c < kGroup; c += 2) {
-              a0 += p[c]; a1 += p[c + 1];
-              extra += ((lastbit >> c) & 1u) ? p[c] : (((lastbit >> (c + 1)) & 1u) ? p[c + 1] : 0.f);
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
+              p[c] = exp2_ftz(x.x);
+              p[c + 1] = exp2_ftz(x.y);
+              acc = __fadd2_rn(acc, make_float2(p[c], p[c + 1]));
             }
-            psum = a0 + a1;
-            // the ragged last block has its own length (:220)
-            wsum = psum * float(kBlock) + extra * float(last_len - kBlock);
           }
+          const float psum = acc.x + acc.y;
+          float extra = 0.f;
+          // bit of the ragged last block's column, if it is in this group
+          // (a bit test, not an index: p[] must stay in registers); the
+          // branch is uniform and taken in one group at most
+          const uint32_t lastbit = (lim >= 1 && lim <= kGroup) ? (1u << (lim - 1)) : 0u;
+          if (lastbit) {
+#pragma unroll
+            for (int c = 0; c < kGroup; ++c) extra += ((lastbit >> c) & 1u) ? p[c] : 0.f;
+          }
+          // the ragged last block has its own length (:220)
+          const float wsum = psum * float(kBlock) + extra * float(last_len - kBlock);
 #pragma unroll
           for (int c = 0; c < kGroup; c += 2) pk[c / 2] = pack_bf16x2(p[c], p[c + 1]);
           gl += wsum * fast_exp2(m_used - m_true_g);
@@ -691,9 +698,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // scores there at step n-2.  (The other set's buffer would not do: at
         // the first group that set may still be reading the full-width
         // scores of step n-1 for its probabilities.)
-        // U = bf16(w q) over all D columns, from this row of Q in shared
-        // memory, built before the wait so that it overlaps the P.V of n-2
+        // U = bf16(q * bf16(w)) over all D columns (one packed bf16 multiply
+        // per column pair), from this row of Q in shared memory, built before
+        // the wait so that it overlaps the P.V of n-2
         uint32_t u[C::kBoxes][32];
+        const __nv_bfloat162 w2 = __float2bfloat162_rn(w);
 #pragma unroll
         for (int bx = 0; bx < C::kBoxes; ++bx) {
 #pragma unroll
@@ -703,8 +712,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
-              const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[x]));
-              u[bx][c * 4 + x] = pack_bf16x2(qf.x * w, qf.y * w);
+              const __nv_bfloat162 prod = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&qw[x]), w2);
+              u[bx][c * 4 + x] = *reinterpret_cast<const uint32_t*>(&prod);
             }
           }
         }
