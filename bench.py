@@ -40,7 +40,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch of the attention kernel from one ncu
 # capture of 4 of the 40 heads (237.4 MB read + 61.3 MB written), scaled by
 # 10 (work and bytes are per head).  Keyed by (workload, kernel).
-ATTN_TRAFFIC_BYTES = {("wan14b-720p", "tcgen05"): 2.987e9}
+ATTN_TRAFFIC_BYTES = {("wan14b-720p", "tcgen05"): 2.994e9}
 
 
 def parse():
