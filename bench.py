@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--config", default="wan14b-720p")
     ap.add_argument("--impl", default="pasa_b200", choices=["pasa_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
-    ap.add_argument("--e2e-chunk", type=int, default=2, help="heads per chunk of the end-to-end host pipeline")
+    ap.add_argument("--e2e-chunk", type=int, default=1, help="heads per chunk of the end-to-end host pipeline")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tcgen05", "simt"])
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads (small profiling cases)")
