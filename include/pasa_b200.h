@@ -182,8 +182,10 @@ PASA_API int pasa_forward_ex(void* stream, const void* q, const void* k, const v
  *     PASA_ERR_WORKSPACE without launching anything.  At D=128, bf16 and
  *     density 0.1 that allows about 11 heads of 75600 tokens per call.
  *   - The first call on a device resolves the array's device address
- *     (cudaGetSymbolAddress) and caches it.  Make that first call before
- *     any stream capture.
+ *     (cudaGetSymbolAddress) and caches it per CUDA context; a call from
+ *     another context (one the caller created, or the primary context
+ *     again after cudaDeviceReset) resolves it anew.  Make the first call
+ *     in each context before any stream capture.
  *   - Every call on a device shares the one array, which keeps the last
  *     call's contents.  Calls whose work overlaps on the GPU (for example on
  *     two streams at once) race on it and must be serialised by the caller.
@@ -210,6 +212,12 @@ PASA_API int pasa_forward_noalloc(void* stream, const void* q, const void* k, co
  *     256-byte aligned, not used by anything else during the call.
  *   - noise_h: NULL, or host [B*H, NT] floats as in pasa_select.
  *   - err_bits (nullable, host): the OR of the chunks' PASA_DEVERR_* bits.
+ *   - The three streams and their events belong to the library, one set
+ *     per device, created on the first call and kept until the process
+ *     exits (they do not survive cudaDeviceReset).  Concurrent calls on
+ *     one device from several host threads are correct but share these
+ *     streams, so they run one after the other on the GPU and each call's
+ *     final wait also waits for the others' queued work.
  */
 PASA_API int pasa_forward_host_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype,
                  double density, int64_t heads_per_chunk, size_t* bytes);

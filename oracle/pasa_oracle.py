@@ -205,7 +205,7 @@ def select_blocks(qc, kc, h_norm, scale, top_k, dtype="bf16", use_cov_bias=True,
 # ---------------------------------------------------------------------------
 def attention(q, k, v, kc, vc, h_group, indices, scale: float, T: int,
               block: int = 64, group: int = 32, dtype: str = "bf16",
-              qblocks=None, rescale_gl: bool = False) -> np.ndarray:
+              qblocks=None, rescale_gl: bool = False, first_order: str = "reference") -> np.ndarray:
     """Exact attention over the selected blocks, zero-order + per-group
     first-order correction over the rest, one online-softmax pass.
 
@@ -216,6 +216,11 @@ def attention(q, k, v, kc, vc, h_group, indices, scale: float, T: int,
     are returned as zeros.  ``rescale_gl=True`` is a deliberately WRONG
     variant (g_l rescaled with the running max) used only by tests to show
     that a fixture exercises the reference's unrescaled g_l.
+    ``first_order="rounded_operand"`` is a measuring variant, not the
+    reference: it forms the first-order term the way the tensor-core kernel
+    does, as bf16(q * bf16(w)) times H_g with w = scale * (sum of the group's
+    probabilities), instead of (q H_g) * w in fp32 (:251-253); tests use it
+    to size that rounding against the tolerance.
     """
     BH, _, D = q.shape
     qb, kb, vb = (_blocks(np.asarray(a, np.float32), block) for a in (q, k, v))
@@ -278,9 +283,14 @@ def attention(q, k, v, kc, vc, h_group, indices, scale: float, T: int,
             acc = (acc + np.matmul(to_dtype(p, dtype), vcp[cols]).astype(np.float32)).astype(np.float32)
             # g_l is accumulated without the alpha rescale, exactly as :242-243
             g_l = (g_l + (p * lens_all[cols]).sum(axis=-1, dtype=np.float32)).astype(np.float32)
-            r = np.matmul(Q, h_group[bh, g]).astype(np.float32)  # :251
             gps = p.sum(axis=-1, dtype=np.float32)  # :252
-            acc = (acc + r * (gps * scale32)[..., None]).astype(np.float32)  # :253
+            if first_order == "rounded_operand":
+                w = to_dtype((gps * scale32).astype(np.float32), "bf16")
+                u = to_dtype((Q * w[..., None]).astype(np.float32), "bf16")
+                acc = (acc + np.matmul(u, h_group[bh, g]).astype(np.float32)).astype(np.float32)
+            else:
+                r = np.matmul(Q, h_group[bh, g]).astype(np.float32)  # :251
+                acc = (acc + r * (gps * scale32)[..., None]).astype(np.float32)  # :253
 
         # Final (:258-262)
         l_i = (l_i + g_l).astype(np.float32)

@@ -5,8 +5,14 @@
 //
 // The array is a file-scope __device__ variable.  In host code its name is
 // only a host-side stand-in, not a device address, so the device address is
-// looked up with cudaGetSymbolAddress once per device (with that device
-// current) and cached; kernels receive that address.
+// looked up with cudaGetSymbolAddress with the device current and cached;
+// kernels receive that address.  The cache is keyed by the current CUDA
+// context (a context created by the caller, or the device's primary context
+// after a cudaDeviceReset, has its own copy of the module and its own
+// address), so a changed context resolves the address again.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cmath>
 #include <mutex>
 
@@ -22,7 +28,25 @@ __device__ __align__(256) unsigned char g_pasa_noalloc_scratch[kNoAllocScratchBy
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchEntry {
+  CUcontext ctx = nullptr;
+  void* addr = nullptr;
+};
+ScratchEntry g_scratch[kMaxDevices];
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links
+// only the CUDA runtime), looked up once.
+PFN_cuCtxGetCurrent_v4000 ctx_get_current_fn() {
+  static const PFN_cuCtxGetCurrent_v4000 fn = []() -> PFN_cuCtxGetCurrent_v4000 {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    return nullptr;
+  }();
+  return fn;
+}
 
 }  // namespace
 
@@ -42,14 +66,26 @@ extern "C" PASA_API int pasa_forward_noalloc(void* stream, const void* q, const 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PASA_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return PASA_ERR_DEVICE;
+  auto get_ctx = ctx_get_current_fn();
+  CUcontext ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS) return PASA_ERR_CUDA;
   void* scratch = nullptr;
+  if (!ctx) {
+    // No context bound to this thread yet: the runtime binds the device's
+    // primary context on its first call that needs one (this lookup), and
+    // that is the context the launches below use.
+    if (cudaGetSymbolAddress(&scratch, g_pasa_noalloc_scratch) != cudaSuccess || !scratch) return PASA_ERR_CUDA;
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return PASA_ERR_CUDA;
+  }
   {
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    scratch = g_scratch_addr[dev];
-    if (!scratch) {  // first call on this device: resolve the array's device address
+    ScratchEntry& e = g_scratch[dev];
+    if (e.ctx != ctx || !e.addr) {  // first call in this context: resolve the array's device address
       if (cudaGetSymbolAddress(&scratch, g_pasa_noalloc_scratch) != cudaSuccess || !scratch) return PASA_ERR_CUDA;
-      g_scratch_addr[dev] = scratch;
+      e.ctx = ctx;
+      e.addr = scratch;
     }
+    scratch = e.addr;
   }
   // pasa_forward writes every scratch region it reads and clears the error
   // word itself, so the previous call's contents do not matter.
