@@ -58,6 +58,21 @@ namespace pasa {
 
 namespace tc {
 
+// K and V ring depths (slots of two key blocks) and how many phase-1 steps
+// the producer issues K ahead of V.
+#ifndef PASA_ATTN_SK
+#define PASA_ATTN_SK 3
+#endif
+#ifndef PASA_ATTN_SV
+#define PASA_ATTN_SV 2
+#endif
+#ifndef PASA_ATTN_KV_LAG
+#define PASA_ATTN_KV_LAG 2
+#endif
+#ifndef PASA_ATTN_LAG_H
+#define PASA_ATTN_LAG_H 2
+#endif
+
 constexpr int kSetWarps = 4;               // warps per softmax set (one per TMEM lane quadrant)
 constexpr int kSoftmaxWarps = 2 * kSetWarps;
 constexpr int kThreads = 32 * (3 + kSoftmaxWarps);  // TMA, S issuer, P.V issuer, two softmax sets
@@ -75,8 +90,8 @@ struct Cfg {
   static constexpr int kPairBytes = kBoxes * kRowBox;   // K (or V) of two key blocks
   static constexpr int kCBytes = kGroup * D * 2;        // kc (or vc) rows of one group
   static constexpr int kHBytes = D * D * 2;
-  static constexpr int kSK = 3;                         // K ring slots
-  static constexpr int kSV = 2;                         // V ring slots
+  static constexpr int kSK = PASA_ATTN_SK;              // K ring slots
+  static constexpr int kSV = PASA_ATTN_SV;              // V ring slots
   static constexpr int kKVRegion = (kSK + kSV) * kPairBytes;
   // Phase 2 has two rings, aliased on the K and V rings: kc rows (read by
   // the score MMAs) and vc rows + H (read by the P.V issuer).  Each is
@@ -86,7 +101,7 @@ struct Cfg {
   static constexpr int kSH = 3;                         // vc/H ring slots
   static constexpr int kSCFit = (kKVRegion - kSH * kSlotH) / kCBytes;
   static constexpr int kSC = kSCFit < 8 ? kSCFit : 8;   // kc ring slots
-  static constexpr int kLagH = 2;                       // kc loads run this many groups ahead of vc/H
+  static constexpr int kLagH = PASA_ATTN_LAG_H;         // kc loads run this many groups ahead of vc/H
   // TMEM columns
   static constexpr uint32_t kColO = 0;
   static constexpr uint32_t kColP = 128;                // P region b at kColP + 64 b
@@ -136,7 +151,7 @@ struct Params {
 // Optional step tracer (compile with -DPASA_TRACE): one CTA, chosen with
 // pasa_trace_select(), records SM clock stamps of its pipeline events for
 // the first kTraceSteps steps into g_pasa_trace[event][step]: 0 producer
-// issue (K), 1 S issue, 28 S issued, 2 P.V issue, 29 P.V issued, 3 K landed,
+// issue (K), 1 S issue, 28 S issued, 2 P.V issue, 29 P.V issued, 3 V issue,
 // 4+w softmax warp w (0-7) sees S, 12+w softmax warp w done, 20-27 set-0
 // sub-stages; pasa_trace_read() copies them out.
 #ifdef PASA_TRACE
@@ -144,6 +159,15 @@ constexpr int kTraceSteps = 1024;
 __device__ unsigned long long g_pasa_trace[30][kTraceSteps];
 __device__ unsigned int g_pasa_trace_cta[2];  // (blockIdx.x, blockIdx.y) of the traced CTA
 __device__ unsigned long long g_pasa_trace_ctl[8];  // entry, set-up done, softmax done, exit (per traced CTA)
+// every CTA: global timer (ns) at entry and exit, SM clock cycles from entry
+// to exit, SM id and union size, at [blockIdx.y * gridDim.x + blockIdx.x]
+constexpr int kTraceCtas = 65536;
+__device__ unsigned long long g_pasa_trace_cta_rec[kTraceCtas][4];
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 #define PASA_TRACE_CTL(i) do { if (pasa_traced) g_pasa_trace_ctl[(i)] = clock64(); } while (0)
 // pasa_traced: a bool computed once per CTA at kernel entry
 #define PASA_TRACE_MARK(ev, step)                                                        \
@@ -197,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 #ifdef PASA_TRACE
   const bool pasa_traced = blockIdx.x == g_pasa_trace_cta[0] && blockIdx.y == g_pasa_trace_cta[1];
   if (tid == 0) PASA_TRACE_CTL(0);
+  const unsigned long long pasa_t0_ns = global_ns(), pasa_t0_clk = clock64();
 #endif
   const int64_t pair = blockIdx.x, bh = blockIdx.y;
   const int64_t NT = P.NT, NG = P.NG;
@@ -307,12 +332,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
 
   if (warp == 0) {
     // ================= TMA producer =================
-#ifdef PASA_TRACE
-    if (lane == 1 && pasa_traced) {  // trace only: stamp K arrival (event 3)
-      for (int64_t n = 0; n < nP && n < kTraceSteps; ++n)
-        if (mbar_wait_bounded(&full_k[n % C::kSK], uint32_t((n / C::kSK) & 1), kPollLimit)) PASA_TRACE_MARK(3, n);
-    }
-#endif
     if (lane == 0) {
       bool ok = true;
       const int32_t row0 = int32_t(pair * kRowsPerTile);
@@ -338,13 +357,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       auto load_v = [&](int64_t p) {
         const int s = int(p % C::kSV);
         if (!mbar_wait_bounded(&empty_v[s], uint32_t((p / C::kSV) & 1) ^ 1u, kPollLimit)) { ok = false; return; }
+        PASA_TRACE_MARK(3, p);
         load_pair(&maps.v, sm + C::kOffV + s * C::kPairBytes, &full_v[s], p);
       };
       // K runs two steps ahead of V in issue order, so a V slot still held by
       // a P.V never holds back the K that the score MMAs need next.
-      for (int64_t p = 0; p < nP + 2 && ok; ++p) {
+      for (int64_t p = 0; p < nP + PASA_ATTN_KV_LAG && ok; ++p) {
         if (p < nP) load_k(p);
-        if (ok && p >= 2) load_v(p - 2);
+        if (ok && p >= PASA_ATTN_KV_LAG) load_v(p - PASA_ATTN_KV_LAG);
       }
       // ring 2 aliases the K and V rings: all of them must be free
       for (int64_t p = (nP > C::kSK ? nP - C::kSK : 0); p < nP && ok; ++p)
@@ -581,11 +601,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         float mx = -INFINITY;
         if (act0) { load_block(0, last0); mx = fmaxf(max_tree32(sa), max_tree32(sb)); }
         if (act1) { load_block(1, last1); mx = fmax3(mx, max_tree32(sa), max_tree32(sb)); }
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(24, n);
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(24, n);
         mx *= sm_scale;  // max commutes with the positive scale
         float m_prev = m_used;
         if (live) advance_max(n, mx, m_prev);  // uniform per lane quadrant
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(25, n);
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(25, n);
         const bool need = (m_used != m_prev) && (m_prev != -INFINITY);
         if (__any_sync(0xffffffffu, need)) rescale_o(n, need ? fast_exp2(m_prev - m_used) : 1.0f);
         if (m_applied != m_used) {
@@ -624,12 +644,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         }
         // this set's P region was last read by the P.V of step n-2
         if (n >= 2) { wait_bar(&o_done[n & 1], (n - 2) >> 1); tc_fence_after(); }
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(26, n);
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(26, n);
         tmem_st16(tP, p0a);
         tmem_st16(tP + 16, p0b);
         tmem_st16(tP + 32, p1a);
         tmem_st16(tP + 48, p1b);
-        if (warp == 3 && lane == 0) PASA_TRACE_MARK(27, n);
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(27, n);
         tmem_wait_st();
       } else {
         // ---------------- Phase 2: group g ----------------
@@ -655,6 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           mx = (mx == -INFINITY) ? mx : mx * sm_scale;
           float m_prev = m_used;
           advance_max(n, mx, m_prev);
+          if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(25, n);
           const float m_true_g = m_true;  // the reference's m at this group (:237, :243)
           const bool grow = m_used != m_prev;  // m_used is finite for live rows here
           if (__any_sync(0xffffffffu, grow)) rescale_o(n, grow ? fast_exp2(m_prev - m_used) : 1.0f);
@@ -717,11 +738,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             }
           }
         }
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(24, n);
         if (n >= 2) { wait_bar(&o_done[n & 1], (n - 2) >> 1); tc_fence_after(); }
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(26, n);
         tmem_st16(tP, pk);
 #pragma unroll
         for (int bx = 0; bx < C::kBoxes; ++bx) tmem_st32(tU + bx * 32, u[bx]);
         tmem_wait_st();
+        if ((warp & 3) == 3 && lane == 0) PASA_TRACE_MARK(27, n);
       }
       // hand P (and U) of step n to the P.V issuer
       tc_fence_before();
@@ -789,6 +813,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   tc_fence_before();
   __syncthreads();
   if (tid == 0) PASA_TRACE_CTL(3);
+#ifdef PASA_TRACE
+  if (tid == 0) {
+    const unsigned long long idx = (unsigned long long)blockIdx.y * gridDim.x + blockIdx.x;
+    if (idx < kTraceCtas) {
+      unsigned int smid;
+      asm volatile("mov.u32 %0, %smid;" : "=r"(smid));
+      g_pasa_trace_cta_rec[idx][0] = pasa_t0_ns;
+      g_pasa_trace_cta_rec[idx][1] = global_ns();
+      g_pasa_trace_cta_rec[idx][2] = clock64() - pasa_t0_clk;
+      g_pasa_trace_cta_rec[idx][3] = ((unsigned long long)smid << 32) | (unsigned long long)nU;
+    }
+  }
+#endif
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
@@ -874,6 +911,9 @@ extern "C" PASA_API int pasa_trace_read(void* host_dst, size_t bytes) {
 }
 extern "C" PASA_API int pasa_trace_ctl_read(void* host_dst, size_t bytes) {
   return cudaMemcpyFromSymbol(host_dst, pasa::tc::g_pasa_trace_ctl, bytes) == cudaSuccess ? 0 : PASA_ERR_CUDA;
+}
+extern "C" PASA_API int pasa_trace_cta_read(void* host_dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(host_dst, pasa::tc::g_pasa_trace_cta_rec, bytes) == cudaSuccess ? 0 : PASA_ERR_CUDA;
 }
 extern "C" PASA_API int pasa_trace_select(unsigned int x, unsigned int y) {
   const unsigned int v[2] = {x, y};
