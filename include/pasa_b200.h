@@ -227,6 +227,41 @@ PASA_API int pasa_forward_host(void* stream, const void* q_h, const void* k_h, c
                  void* workspace, size_t workspace_bytes, int64_t heads_per_chunk,
                  void* o_h, uint32_t* err_bits, int kernel);
 
+/* Emulated-mask layouts of the head classification (pasa_sample_mse). */
+typedef enum pasa_model {
+  PASA_MODEL_HUNYUAN = 0,  /* band of floor(1.5 * frame_size / 128) blocks of 128
+                              tokens; the context_length text tokens at the tail
+                              attend and are attended by everything
+                              (svg/models/hyvideo/utils.py:48-94)              */
+  PASA_MODEL_WAN = 1       /* band of floor(2 * frame_size / 128) blocks plus the
+                              first frame as a sink; no text tokens
+                              (svg/models/wan/utils.py:63-110)                 */
+} pasa_model;
+
+/*
+ * Spatial / temporal head classification.  Replaces sample_mse
+ * (svg/models/hyvideo/attention.py:381-405; Wan twin
+ * svg/models/wan/attention.py:264-288) and the emulated masks it indexes
+ * (get_attention_mask, evaluated in closed form instead of as dense T x T
+ * tensors).  For each of the n_rows sampled query positions `rows` (host
+ * int64, 1 <= n_rows <= 32, each in [0, T) -- the reference's
+ * torch.randint draw), the attention output under the spatial mask, the
+ * temporal mask (the spatial band in token-major order) and no mask, with
+ * the reference's roundings in the input dtype; then per head the mean
+ * squared difference of each masked output from the unmasked one.
+ *   q, k, v        [cfg, H, T, D] device, T = context_length +
+ *                  num_frame * frame_size (context_length 0 for Wan)
+ *   mse            [2, cfg, H] in the input dtype (spatial, temporal), or NULL
+ *   best_mask_idx  [cfg, H] int32 argmin (0 spatial, 1 temporal; ties 0), or NULL
+ *   workspace      device, pasa_sample_mse_workspace_size() bytes, 256-byte aligned
+ */
+PASA_API int pasa_sample_mse_workspace_size(int64_t BH, int64_t T, int D, size_t* bytes);
+PASA_API int pasa_sample_mse(void* stream, const void* q, const void* k, const void* v,
+                 int64_t cfg, int64_t H, int64_t T, int D, int dtype,
+                 const int64_t* rows, int64_t n_rows, int model,
+                 int64_t context_length, int64_t num_frame, int64_t frame_size,
+                 void* workspace, size_t workspace_bytes, void* mse, int32_t* best_mask_idx);
+
 /*
  * Token-layout permutation of the temporal heads (frame-major <-> token-
  * major), text tail untouched.  Replaces hunyuan_sparse_head_placement

@@ -36,6 +36,9 @@ DEVERR_WAIT_TIMEOUT = 0x1
 O_BHTD = 0
 O_BTHD = 1
 
+MODEL_HUNYUAN = 0
+MODEL_WAN = 1
+
 PEER_HANDLE_BYTES = 64
 
 EXPORTS = (
@@ -44,6 +47,7 @@ EXPORTS = (
     "pasa_forward_host_workspace_size", "pasa_forward_host", "pasa_dense_attn",
     "pasa_dit_row_norm", "pasa_dit_qkv_rope", "pasa_forward_ex", "pasa_peer_alloc", "pasa_peer_free",
     "pasa_peer_open", "pasa_peer_close", "pasa_dit_qkv_rope_scatter", "pasa_forward_scatter",
+    "pasa_sample_mse_workspace_size", "pasa_sample_mse",
 )
 
 _lib = None
@@ -91,6 +95,9 @@ def load() -> ctypes.CDLL:
                                               c_int]),
         "pasa_forward_scatter": (c_int, [P, P, P, P, c_int64, c_int64, c_int, c_double, c_float, c_int, P, P,
                                          c_size_t, P, c_int, c_int64, c_int64, c_int]),
+        "pasa_sample_mse_workspace_size": (c_int, [c_int64, c_int64, c_int, POINTER(c_size_t)]),
+        "pasa_sample_mse": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, P, c_int64, c_int,
+                                    c_int64, c_int64, c_int64, P, c_size_t, P, P]),
         "pasa_dit_row_norm": (c_int, [P, P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_float, c_int, P]),
         "pasa_dit_qkv_rope": (c_int, [P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, c_int,
                                       P, P, P]),

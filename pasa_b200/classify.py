@@ -1,98 +1,82 @@
-"""Spatial / temporal head classification (the SVG profiling step).
+"""Spatial / temporal head classification on the GPU (the SVG profiling
+step that decides which heads the token placement reorders).
 
-Restates ``sample_mse`` (svg/models/hyvideo/attention.py:381-405, Wan twin
-svg/models/wan/attention.py:264-288) with the emulated masks of
-``get_attention_mask`` (svg/models/hyvideo/utils.py:48-94,
-svg/models/wan/utils.py:63-110).  The reference builds each mask as a dense
-T x T tensor on the CPU with a Python double loop (4.3 GB at T=32760) and
-then indexes the sampled rows.  Here the two masks are evaluated in closed
-form for the sampled rows only:
-
-* spatial: keys within ``thres // 128`` 128-token blocks of the query block,
-  with ``thres = 1.5 * frame_size`` (HunyuanVideo) or ``2 * frame_size``
-  (Wan).  HunyuanVideo keeps the trailing ``context_length`` text tokens
-  fully visible in both directions.  Wan adds a first-frame sink
-  (keys < frame_size).
-* temporal: the spatial mask of the token-major layout.  Position
-  f*S + p maps to p*F + f, from the reference's
-  ``reshape(S, F, S, F).permute(1, 0, 3, 2)``.
-
-``sample_mse`` consumes the CPU random generator exactly as the reference
-does (``torch.randint(0, sample_mse_max_row, (rows,))``).  It returns the
-per-head MSE of each masked softmax output against the full softmax output,
-``[2, cfg, H]``.  ``classify_heads`` takes the argmin (0 spatial,
-1 temporal), which is the ``best_mask_idx`` that the placement functions
-consume.
+``sample_mse`` keeps the meaning of the reference's
+``sample_mse`` (svg/models/hyvideo/attention.py:381-405; Wan twin
+svg/models/wan/attention.py:264-288): for ``num_sampled_rows`` query rows
+drawn with ``torch.randint(0, sample_mse_max_row, (n,))`` on the CPU
+generator (the reference's own draw), the mean squared difference between
+attention under each emulated mask (spatial, temporal; get_attention_mask,
+svg/models/hyvideo/utils.py:48-94 and svg/models/wan/utils.py:63-110) and
+full attention, per head: ``[2, cfg, H]`` in the query dtype.  The work
+runs in ``pasa_sample_mse`` (csrc/classify.cu), which evaluates the masks
+in closed form instead of building dense T x T tensors.  ``classify_heads``
+returns the argmin, the ``best_mask_idx`` the placement functions consume
+(0 spatial, 1 temporal).
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
-import torch.nn.functional as F
 
-MASKS = ("spatial", "temporal")
+from . import _lib
+from .ops import _dtype_code, _stream_ptr
 
-
-def _band(qi: torch.Tensor, ki: torch.Tensor, frame_size: int, factor: float) -> torch.Tensor:
-    """|qi//128 - ki//128| < (factor * frame_size) // 128, elementwise with broadcasting."""
-    width = int((factor * frame_size) // 128)
-    return (torch.div(qi, 128, rounding_mode="floor") - torch.div(ki, 128, rounding_mode="floor")).abs() < width
+_MODELS = {"hunyuan": _lib.MODEL_HUNYUAN, "wan": _lib.MODEL_WAN}
 
 
-def emulated_mask_rows(rows: torch.Tensor, mask_name: str, model: str, context_length: int, num_frame: int,
-                       frame_size: int) -> torch.Tensor:
-    """Rows ``rows`` of the emulated attention mask, as a bool [R, T] tensor.
-
-    ``model`` is "hunyuan" (text tokens at the tail, hyvideo/utils.py:48-94)
-    or "wan" (no text tokens, first-frame sink, wan/utils.py:63-110)."""
-    device = rows.device
-    V = num_frame * frame_size
-    T = V + (context_length if model == "hunyuan" else 0)
-    keys = torch.arange(T, device=device)
-    q = rows.to(torch.int64)[:, None]
-    k = keys[None, :]
-
-    def token_major(x):  # frame-major position f*S + p -> token-major p*F + f
-        f = torch.div(x, frame_size, rounding_mode="floor")
-        p = x - f * frame_size
-        return p * num_frame + f
-
-    if mask_name == "temporal":
-        qm, km = token_major(torch.clamp(q, max=V - 1)), token_major(torch.clamp(k, max=V - 1))
-    elif mask_name == "spatial":
-        qm, km = q, k
-    else:
-        raise ValueError(f"unknown mask {mask_name!r}")
-    if model == "hunyuan":
-        m = _band(qm, km, frame_size, 1.5)
-        video = (q < V) & (k < V)
-        return torch.where(video, m, torch.ones_like(m))  # text rows and columns are all ones
-    if model == "wan":
-        return _band(qm, km, frame_size, 2.0) | (km < frame_size)  # + first-frame sink
-    raise ValueError(f"unknown model {model!r}")
+def _run(query, key, value, model, context_length, num_frame, frame_size, num_sampled_rows, sample_mse_max_row,
+         rows):
+    for name, t in (("query", query), ("key", key), ("value", value)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dim() != 4:
+            raise ValueError(f"{name} must be a [cfg, H, T, D] CUDA tensor")
+    if key.shape != query.shape or value.shape != query.shape:
+        raise ValueError("query, key and value must have one shape")
+    if key.dtype != query.dtype or value.dtype != query.dtype:
+        raise ValueError("query, key and value must have one dtype")
+    if model not in _MODELS:
+        raise ValueError(f"model is one of {sorted(_MODELS)}")
+    query, key, value = query.contiguous(), key.contiguous(), value.contiguous()
+    cfg, H, T, D = query.shape
+    ctx = context_length if model == "hunyuan" else 0
+    if frame_size is None:
+        frame_size = (T - ctx) // num_frame
+    if rows is None:
+        n = min(num_sampled_rows, T)
+        rows = torch.randint(low=0, high=sample_mse_max_row, size=(n,))  # CPU generator, as the reference
+    rows = rows.to(device="cpu", dtype=torch.int64).contiguous()
+    dcode = _dtype_code(query)
+    lib = _lib.load()
+    with torch.cuda.device(query.device):
+        nb = ctypes.c_size_t()
+        _lib.check("pasa_sample_mse_workspace_size",
+                   lib.pasa_sample_mse_workspace_size(cfg * H, T, D, ctypes.byref(nb)))
+        ws = torch.empty(nb.value, dtype=torch.uint8, device=query.device)
+        mse = torch.empty((2, cfg, H), dtype=query.dtype, device=query.device)
+        best = torch.empty((cfg, H), dtype=torch.int32, device=query.device)
+        _lib.check("pasa_sample_mse", lib.pasa_sample_mse(
+            _stream_ptr(query.device), query.data_ptr(), key.data_ptr(), value.data_ptr(), cfg, H, T, D, dcode,
+            rows.data_ptr(), rows.numel(), _MODELS[model], ctx, num_frame, frame_size, ws.data_ptr(), nb.value,
+            mse.data_ptr(), best.data_ptr()))
+    return mse, best
 
 
 def sample_mse(query, key, value, *, model="hunyuan", context_length=0, num_frame=1, frame_size=None,
-               num_sampled_rows=32, sample_mse_max_row=10000, masks=MASKS):
-    """Per-head MSE of each emulated sparse mask against full attention on
-    sampled query rows; [len(masks), cfg, H] in the query dtype."""
-    cfg, num_heads, seq_len, dim = query.size()
-    if frame_size is None:
-        frame_size = (seq_len - (context_length if model == "hunyuan" else 0)) // num_frame
-    n = min(num_sampled_rows, seq_len)
-    sampled_rows = torch.randint(low=0, high=sample_mse_max_row, size=(n,))  # CPU generator, like the reference
-    rows_dev = sampled_rows.to(query.device)
-    sampled_q = query[:, :, rows_dev, :]
-    scores = torch.matmul(sampled_q, key.transpose(-2, -1)) / (dim ** 0.5)
-    golden = torch.matmul(F.softmax(scores, dim=-1), value)
-    out = torch.zeros(len(masks), cfg, num_heads, device=query.device, dtype=query.dtype)
-    for i, name in enumerate(masks):
-        m = emulated_mask_rows(rows_dev, name, model, context_length, num_frame, frame_size)
-        masked = scores.masked_fill(~m, float("-inf"))
-        hs = torch.matmul(F.softmax(masked, dim=-1), value)
-        out[i] = torch.mean((hs - golden) ** 2, dim=(2, 3))
-    return out
+               num_sampled_rows=32, sample_mse_max_row=10000, rows=None):
+    """Per-head MSE of the spatial and temporal emulated masks against full
+    attention on sampled query rows: ``[2, cfg, H]`` in the query dtype.
+    ``rows`` (CPU int64, at most 32) replaces the random draw when given."""
+    return _run(query, key, value, model, context_length, num_frame, frame_size, num_sampled_rows,
+                sample_mse_max_row, rows)[0]
 
 
 def classify_heads(query, key, value, **kw) -> torch.Tensor:
-    """best_mask_idx [cfg, H]: 0 = spatial head, 1 = temporal head."""
-    return torch.argmin(sample_mse(query, key, value, **kw), dim=0)
+    """best_mask_idx [cfg, H] (int64, as torch.argmin): 0 spatial head, 1
+    temporal head; equal MSEs pick spatial, as torch.argmin picks the first."""
+    args = [kw.pop(n, d) for n, d in (("model", "hunyuan"), ("context_length", 0), ("num_frame", 1),
+                                       ("frame_size", None), ("num_sampled_rows", 32),
+                                       ("sample_mse_max_row", 10000), ("rows", None))]
+    if kw:
+        raise TypeError(f"unexpected arguments {sorted(kw)}")
+    return _run(query, key, value, *args)[1].long()

@@ -20,6 +20,9 @@ cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const vo
                            int64_t, const OutScatter&);
 cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
                          int64_t, int64_t, int64_t, int);
+size_t sample_mse_workspace(int64_t BH, int64_t T, int D);
+cudaError_t launch_sample_mse(cudaStream_t, int, int, const void*, const void*, const void*, int64_t, int64_t,
+                              const int64_t*, int, int, int64_t, int64_t, int64_t, void*, void*, int32_t*);
 int dit_max_cols();
 cudaError_t launch_row_norm(cudaStream_t, const void*, const void*, const float*, void*, const float*, const float*,
                             const float*, const float*, int64_t, int64_t, int, float, int, int, void*);
@@ -286,6 +289,42 @@ int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, i
   // the block statistics are not read in dense mode; q stands in for their (unused) tensor maps
   return cuda_status(launch_attn_tc(static_cast<cudaStream_t>(stream), D, q, k, v, q, q, q, nullptr, BH, T,
                                     cdiv(T, kBlock), scale, o, err_word, 1, 0, OutScatter{}));
+}
+
+int pasa_sample_mse_workspace_size(int64_t BH, int64_t T, int D, size_t* bytes) {
+  if (!bytes) return PASA_ERR_NULL;
+  if (BH < 1 || BH > 65535 || T < 1) return PASA_ERR_SHAPE;
+  if (D != 64 && D != 128) return PASA_ERR_UNSUPPORTED;
+  *bytes = sample_mse_workspace(BH, T, D);
+  return PASA_OK;
+}
+
+int pasa_sample_mse(void* stream, const void* q, const void* k, const void* v, int64_t cfg, int64_t H, int64_t T,
+                    int D, int dtype, const int64_t* rows, int64_t n_rows, int model, int64_t context_length,
+                    int64_t num_frame, int64_t frame_size, void* workspace, size_t workspace_bytes, void* mse,
+                    int32_t* best_mask_idx) {
+  if (dtype != PASA_BF16 && dtype != PASA_F32) return PASA_ERR_DTYPE;
+  if (D != 64 && D != 128) return PASA_ERR_UNSUPPORTED;
+  if (model != PASA_MODEL_HUNYUAN && model != PASA_MODEL_WAN) return PASA_ERR_UNSUPPORTED;
+  if (cfg < 1 || H < 1 || cfg * H > 65535 || T < 1) return PASA_ERR_SHAPE;
+  if (n_rows < 1 || n_rows > 32) return PASA_ERR_SHAPE;
+  if (context_length < 0 || num_frame < 1 || frame_size < 1) return PASA_ERR_SHAPE;
+  // the sequence is the video (plus the text tail for HunyuanVideo), as the
+  // processors assert (hyvideo/attention.py:491-494, wan/attention.py:359-362)
+  // (Wan's mask has no text tail: its temporal reshape needs T = num_frame *
+  // frame_size, wan/utils.py:99-103)
+  if (model == PASA_MODEL_WAN && context_length != 0) return PASA_ERR_UNSUPPORTED;
+  if (context_length + num_frame * frame_size != T) return PASA_ERR_SHAPE;
+  if (!q || !k || !v || !rows || !workspace || (!mse && !best_mask_idx)) return PASA_ERR_NULL;
+  for (int64_t r = 0; r < n_rows; ++r)
+    if (rows[r] < 0 || rows[r] >= T) return PASA_ERR_SHAPE;  // the reference's indexing would fail too
+  if (workspace_bytes < sample_mse_workspace(cfg * H, T, D)) return PASA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PASA_ERR_ALIGN;
+  int st = check_device();
+  if (st) return st;
+  return cuda_status(launch_sample_mse(static_cast<cudaStream_t>(stream), dtype, D, q, k, v, cfg * H, T, rows,
+                                       int(n_rows), model, context_length, num_frame, frame_size, workspace, mse,
+                                       best_mask_idx));
 }
 
 int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal, int64_t cfg, int64_t H,

@@ -1,0 +1,359 @@
+// Head classification on the GPU: per head, the mean squared difference
+// between attention under each emulated sparse mask (spatial, temporal) and
+// full attention, on a few sampled query rows.  Replaces sample_mse
+// (svg/models/hyvideo/attention.py:381-405; the Wan twin at
+// svg/models/wan/attention.py:264-288) together with the emulated masks of
+// get_attention_mask (svg/models/hyvideo/utils.py:48-94,
+// svg/models/wan/utils.py:63-110), which the reference builds as dense T x T
+// tensors with a Python double loop.  Here the masks are closed-form
+// predicates on (query, key) positions.
+//
+// Arithmetic follows the reference's torch ops in the input dtype:
+//   s   = round(round(q . k) * (1 / sqrt(D)))        matmul, then / dim**0.5
+//   p   = round(exp(s - M) / L)                      F.softmax (fp32 inside)
+//   h   = round(sum_j p_j v_j)                       matmul (fp32 accumulate)
+//   mse = round(mean(round(round(h_m - h_full)^2)))  torch.mean over rows, D
+// with round() the cast to the input dtype (bf16: nearest even).
+//
+// Four launches: (1) per key chunk, the masked row maxima and exponential
+// sums of the three variants (full, spatial, temporal); (2) their
+// combination per head; (3) per key chunk, the probabilities times V; (4)
+// the sum over chunks in a fixed order, the rounding of the outputs and the
+// two mean squared differences.  Every sum has a fixed order, so the result
+// is deterministic.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace pasa {
+namespace cls {
+
+constexpr int kRows = 32;        // sampled rows (at most)
+constexpr int kVar = 3;          // 0 full, 1 spatial, 2 temporal
+constexpr int kTile = 64;        // keys per shared-memory tile
+constexpr int kChunk = 2048;     // keys per CTA
+constexpr int kThreads = 256;    // 8 warps x 4 rows; lanes take 2 keys of a tile
+
+struct Spec {
+  int64_t T, V, F, S;   // tokens, video tokens, frames, tokens per frame
+  int64_t width;        // band half-width in 128-token blocks
+  int model;            // 0 HunyuanVideo (text tail), 1 Wan (first-frame sink)
+  int R;                // sampled rows
+  int64_t rows[kRows];  // sampled query positions
+  float inv_sqrt_d;
+};
+
+// frame-major position f*S + p -> token-major p*F + f (the reference's
+// reshape(S, F, S, F).permute(1, 0, 3, 2) of the mask)
+__device__ __forceinline__ int64_t token_major(int64_t x, const Spec& m) {
+  const int64_t f = x / m.S;
+  return (x - f * m.S) * m.F + f;
+}
+
+__device__ __forceinline__ bool allowed(int var, int64_t q, int64_t k, const Spec& m) {
+  if (var == 0) return true;
+  int64_t qm = q, km = k;
+  if (var == 2) {
+    qm = token_major(q < m.V ? q : m.V - 1, m);
+    km = token_major(k < m.V ? k : m.V - 1, m);
+  }
+  const int64_t d = qm / 128 - km / 128;
+  const bool band = (d < 0 ? -d : d) < m.width;
+  if (m.model == 0) return (q < m.V && k < m.V) ? band : true;  // text rows and columns attend everything
+  return band || km < m.S;                                        // Wan: first-frame sink
+}
+
+template <typename T>
+__device__ __forceinline__ float rnd(float x) { return Elem<T>::round(x); }
+
+// Scores of this thread's 4 rows x 2 keys of the tile at j0 (rows 4*warp..,
+// keys j0 + lane and j0 + lane + 32), or -inf past T.
+template <typename T, int D>
+__device__ __forceinline__ void tile_scores(const float* qs, const float* ks, int warp, int lane, int64_t j0,
+                                            const Spec& m, float (&s)[4][2]) {
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    const int jl = lane + 32 * kk;
+    const float* kr = ks + jl * (D + 1);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const float* qr = qs + (4 * warp + rr) * D;
+      float dot = 0.f;
+#pragma unroll 8
+      for (int c = 0; c < D; ++c) dot = fmaf(qr[c], kr[c], dot);
+      s[rr][kk] = (j0 + jl < m.T) ? rnd<T>(rnd<T>(dot) * m.inv_sqrt_d) : -INFINITY;
+    }
+  }
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void load_rows(float* qs, const T* q, int64_t bh, const Spec& m) {
+  for (int x = threadIdx.x; x < kRows * D; x += kThreads) {
+    const int r = x / D, c = x % D;
+    qs[x] = (r < m.R) ? Elem<T>::load(q + (bh * m.T + m.rows[r]) * D + c) : 0.f;
+  }
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void load_tile(float* dst, int stride, const T* src, int64_t bh, int64_t j0,
+                                          const Spec& m) {
+  for (int x = threadIdx.x; x < kTile * D; x += kThreads) {
+    const int j = x / D, c = x % D;
+    dst[j * stride + c] = (j0 + j < m.T) ? Elem<T>::load(src + (bh * m.T + j0 + j) * D + c) : 0.f;
+  }
+}
+
+// (1) per chunk: masked maximum and sum of exp(s - max) per (variant, row)
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) mse_stats_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                             const __grid_constant__ Spec m,
+                                                             float2* __restrict__ part) {
+  extern __shared__ float sm[];
+  float* qs = sm;                  // [32][D]
+  float* ks = qs + kRows * D;      // [64][D+1]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bh = blockIdx.y, c = blockIdx.x;
+  load_rows<T, D>(qs, q, bh, m);
+  float mx[4][kVar], sum[4][kVar];
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+    for (int v = 0; v < kVar; ++v) { mx[rr][v] = -INFINITY; sum[rr][v] = 0.f; }
+  const int64_t jend = (c + 1) * kChunk < m.T ? (c + 1) * kChunk : m.T;
+  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile) {
+    __syncthreads();
+    load_tile<T, D>(ks, D + 1, k, bh, j0, m);
+    __syncthreads();
+    float s[4][2];
+    tile_scores<T, D>(qs, ks, warp, lane, j0, m, s);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int r = 4 * warp + rr;
+      if (r >= m.R) continue;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const int64_t j = j0 + lane + 32 * kk;
+        if (j >= m.T) continue;
+#pragma unroll
+        for (int v = 0; v < kVar; ++v) {
+          if (!allowed(v, m.rows[r], j, m)) continue;
+          const float x = s[rr][kk];
+          if (x > mx[rr][v]) {
+            sum[rr][v] = sum[rr][v] * expf(mx[rr][v] - x) + 1.f;
+            mx[rr][v] = x;
+          } else {
+            sum[rr][v] += expf(x - mx[rr][v]);
+          }
+        }
+      }
+    }
+  }
+  // combine the lanes (fixed butterfly order)
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+    for (int v = 0; v < kVar; ++v) {
+      float a = mx[rr][v], b = sum[rr][v];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, a, off), ob = __shfl_xor_sync(0xffffffffu, b, off);
+        const float nm = fmaxf(a, oa);
+        b = (nm == -INFINITY) ? 0.f : b * expf(a - nm) + ob * expf(oa - nm);
+        a = nm;
+      }
+      const int r = 4 * warp + rr;
+      if (lane == 0) part[((bh * gridDim.x + c) * kVar + v) * kRows + r] = make_float2(a, b);
+    }
+}
+
+// (2) per head: the row maxima M and sums L over all chunks
+__global__ void mse_combine_kernel(const float2* __restrict__ part, int64_t nchunks, float2* __restrict__ ml) {
+  const int64_t bh = blockIdx.x;
+  const int t = threadIdx.x;  // v * 32 + r
+  if (t >= kVar * kRows) return;
+  float M = -INFINITY;
+  for (int64_t c = 0; c < nchunks; ++c) M = fmaxf(M, part[(bh * nchunks + c) * kVar * kRows + t].x);
+  float L = 0.f;
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const float2 p = part[(bh * nchunks + c) * kVar * kRows + t];
+    if (p.x != -INFINITY) L += p.y * expf(p.x - M);
+  }
+  ml[bh * kVar * kRows + t] = make_float2(M, L);
+}
+
+// (3) per chunk: sum_j round(exp(s - M) / L) v_j for the three variants
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) mse_pv_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                          const T* __restrict__ v, const __grid_constant__ Spec m,
+                                                          const float2* __restrict__ ml, float* __restrict__ acc_out) {
+  extern __shared__ float sm[];
+  float* qs = sm;                        // [32][D]
+  float* ks = qs + kRows * D;            // [64][D+1]
+  float* vs = ks + kTile * (D + 1);      // [64][D]
+  float* ps = vs + kTile * D;            // [3][32][64]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bh = blockIdx.y, c = blockIdx.x;
+  load_rows<T, D>(qs, q, bh, m);
+  // output elements of this thread: column col of rows rg*16 .. rg*16+15, every variant
+  constexpr int kRG = kThreads / D;         // row groups (2 for D = 128, 4 for D = 64)
+  constexpr int kRPT = kRows / kRG;         // rows per thread
+  const int col = threadIdx.x % D, rg = threadIdx.x / D;
+  float acc[kVar][kRPT];
+#pragma unroll
+  for (int x = 0; x < kVar; ++x)
+#pragma unroll
+    for (int r = 0; r < kRPT; ++r) acc[x][r] = 0.f;
+  float2 mlr[4][kVar];
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+    for (int x = 0; x < kVar; ++x) mlr[rr][x] = ml[(bh * kVar + x) * kRows + 4 * warp + rr];
+  const int64_t jend = (c + 1) * kChunk < m.T ? (c + 1) * kChunk : m.T;
+  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile) {
+    __syncthreads();
+    load_tile<T, D>(ks, D + 1, k, bh, j0, m);
+    load_tile<T, D>(vs, D, v, bh, j0, m);
+    __syncthreads();
+    float s[4][2];
+    tile_scores<T, D>(qs, ks, warp, lane, j0, m, s);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int r = 4 * warp + rr;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const int jl = lane + 32 * kk;
+        const int64_t j = j0 + jl;
+#pragma unroll
+        for (int x = 0; x < kVar; ++x) {
+          float p = 0.f;
+          if (r < m.R && j < m.T && allowed(x, m.rows[r], j, m))
+            p = rnd<T>(expf(s[rr][kk] - mlr[rr][x].x) / mlr[rr][x].y);
+          ps[(x * kRows + r) * kTile + jl] = p;
+        }
+      }
+    }
+    __syncthreads();
+    for (int jl = 0; jl < kTile; ++jl) {
+      const float vj = vs[jl * D + col];
+#pragma unroll
+      for (int x = 0; x < kVar; ++x)
+#pragma unroll
+        for (int r = 0; r < kRPT; ++r) acc[x][r] = fmaf(ps[(x * kRows + rg * kRPT + r) * kTile + jl], vj, acc[x][r]);
+    }
+  }
+#pragma unroll
+  for (int x = 0; x < kVar; ++x)
+#pragma unroll
+    for (int r = 0; r < kRPT; ++r)
+      acc_out[(((bh * gridDim.x + c) * kVar + x) * kRows + rg * kRPT + r) * D + col] = acc[x][r];
+}
+
+// (4) per head: outputs, differences and the two mean squared differences
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) mse_finish_kernel(const float* __restrict__ acc, int64_t nchunks,
+                                                              int R, int64_t BH, T* __restrict__ mse_out,
+                                                              int32_t* __restrict__ best) {
+  __shared__ float red[2][kThreads];
+  const int64_t bh = blockIdx.x;
+  float part[2] = {0.f, 0.f};
+  for (int e = threadIdx.x; e < R * D; e += kThreads) {
+    float h[kVar];
+#pragma unroll
+    for (int x = 0; x < kVar; ++x) {
+      float a = 0.f;
+      for (int64_t c = 0; c < nchunks; ++c) a += acc[((bh * nchunks + c) * kVar + x) * kRows * D + e];
+      h[x] = rnd<T>(a);
+    }
+#pragma unroll
+    for (int x = 1; x < kVar; ++x) {
+      const float d = rnd<T>(h[x] - h[0]);
+      part[x - 1] += rnd<T>(d * d);
+    }
+  }
+  red[0][threadIdx.x] = part[0];
+  red[1][threadIdx.x] = part[1];
+  __syncthreads();
+  for (int w = kThreads / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      red[0][threadIdx.x] += red[0][threadIdx.x + w];
+      red[1][threadIdx.x] += red[1][threadIdx.x + w];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float inv_n = 1.0f / float(R * D);
+    const float a = rnd<T>(red[0][0] * inv_n), b = rnd<T>(red[1][0] * inv_n);
+    if (mse_out) {
+      Elem<T>::store(mse_out + bh, a);       // [2, cfg*H]: spatial
+      Elem<T>::store(mse_out + BH + bh, b);  // temporal
+    }
+    if (best) best[bh] = (b < a) ? 1 : 0;    // argmin, first index on ties
+  }
+}
+
+template <int D>
+size_t stats_smem() { return sizeof(float) * (kRows * D + kTile * (D + 1)); }
+template <int D>
+size_t pv_smem() { return sizeof(float) * (kRows * D + kTile * (D + 1) + kTile * D + kVar * kRows * kTile); }
+
+}  // namespace cls
+
+// workspace: chunk statistics | (M, L) | chunk partial outputs
+size_t sample_mse_workspace(int64_t BH, int64_t T, int D) {
+  const int64_t nc = cdiv(T, cls::kChunk);
+  size_t o = align256(size_t(BH) * nc * cls::kVar * cls::kRows * sizeof(float2));
+  o += align256(size_t(BH) * cls::kVar * cls::kRows * sizeof(float2));
+  o += align256(size_t(BH) * nc * cls::kVar * cls::kRows * D * sizeof(float));
+  return o;
+}
+
+template <typename T, int D>
+static cudaError_t launch_sample_mse_t(cudaStream_t st, const void* q, const void* k, const void* v, int64_t BH,
+                                       const cls::Spec& m, void* ws, void* mse_out, int32_t* best) {
+  using namespace cls;
+  const int64_t nc = cdiv(m.T, kChunk);
+  char* w = static_cast<char*>(ws);
+  float2* part = reinterpret_cast<float2*>(w);
+  w += align256(size_t(BH) * nc * kVar * kRows * sizeof(float2));
+  float2* ml = reinterpret_cast<float2*>(w);
+  w += align256(size_t(BH) * kVar * kRows * sizeof(float2));
+  float* acc = reinterpret_cast<float*>(w);
+  const dim3 grid{unsigned(nc), unsigned(BH), 1u};
+  auto k1 = mse_stats_kernel<T, D>;
+  auto k3 = mse_pv_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(stats_smem<D>()));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pv_smem<D>()));
+  if (e != cudaSuccess) return e;
+  const T* qt = static_cast<const T*>(q);
+  const T* kt = static_cast<const T*>(k);
+  const T* vt = static_cast<const T*>(v);
+  k1<<<grid, kThreads, stats_smem<D>(), st>>>(qt, kt, m, part);
+  mse_combine_kernel<<<unsigned(BH), 128, 0, st>>>(part, nc, ml);
+  k3<<<grid, kThreads, pv_smem<D>(), st>>>(qt, kt, vt, m, ml, acc);
+  mse_finish_kernel<T, D><<<unsigned(BH), kThreads, 0, st>>>(acc, nc, m.R, BH, static_cast<T*>(mse_out), best);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sample_mse(cudaStream_t st, int dtype, int D, const void* q, const void* k, const void* v,
+                              int64_t BH, int64_t T, const int64_t* rows, int R, int model, int64_t ctx,
+                              int64_t num_frame, int64_t frame_size, void* ws, void* mse_out, int32_t* best) {
+  cls::Spec m{};
+  m.T = T;
+  m.V = num_frame * frame_size;
+  m.F = num_frame;
+  m.S = frame_size;
+  // (factor * frame_size) // 128 with factor 1.5 (HunyuanVideo) or 2 (Wan)
+  m.width = (model == 0) ? (3 * frame_size) / 256 : frame_size / 64;
+  m.model = model;
+  m.R = R;
+  for (int r = 0; r < R; ++r) m.rows[r] = rows[r];
+  m.inv_sqrt_d = 1.0f / float(std::sqrt(double(D)));
+  if (dtype == PASA_BF16) {
+    if (D == 64) return launch_sample_mse_t<__nv_bfloat16, 64>(st, q, k, v, BH, m, ws, mse_out, best);
+    return launch_sample_mse_t<__nv_bfloat16, 128>(st, q, k, v, BH, m, ws, mse_out, best);
+  }
+  if (D == 64) return launch_sample_mse_t<float, 64>(st, q, k, v, BH, m, ws, mse_out, best);
+  return launch_sample_mse_t<float, 128>(st, q, k, v, BH, m, ws, mse_out, best);
+}
+
+}  // namespace pasa

@@ -5,7 +5,7 @@ import torch
 import torch.nn.functional as F
 
 from oracle.layout_oracle import dense_attention_mask
-from pasa_b200 import classify
+from oracle import classify_oracle as classify
 
 
 @pytest.mark.parametrize("model,ctx,F_,S", [("hunyuan", 16, 3, 256), ("hunyuan", 40, 5, 384), ("wan", 0, 4, 256),
