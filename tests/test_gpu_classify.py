@@ -41,9 +41,12 @@ def _compare(got, ref, dtype):
     got, ref = got.float().cpu(), ref.float().cpu()
     rtol = 2e-2 if dtype == torch.bfloat16 else 1e-4
     assert torch.isfinite(got).all()
-    torch.testing.assert_close(got, ref, rtol=rtol, atol=0)
+    # an MSE below 1e-30 means the masked and full outputs agree to the last
+    # bit in all but a few elements; such values are bf16 subnormals, whose
+    # flushing differs between libraries
+    torch.testing.assert_close(got, ref, rtol=rtol, atol=1e-30)
     # the class: argmin of the two masks, unless the reference's MSEs are within the tolerance
-    clear = (ref[0] - ref[1]).abs() > rtol * torch.maximum(ref[0], ref[1])
+    clear = (ref[0] - ref[1]).abs() > rtol * torch.maximum(ref[0], ref[1]) + 1e-30
     return clear
 
 
