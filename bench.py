@@ -125,52 +125,176 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle (numpy restatement of the reference) on a sample
+# CPU baseline and reference arm: the oracle (numpy restatement of the
+# reference's PASA forward) on one full head, over all host cores
 # ---------------------------------------------------------------------------
-def cpu_baseline(w, seed=0, target_s=12.0):
-    """Time the oracle on one head: full block statistics and selection, then
-    attention for as many query blocks (spread over the head) as fill about
-    ``target_s`` seconds, measured after a 4-block probe; extrapolate to the
-    whole call (all query blocks of all heads)."""
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _shm_put(arr, keep):
+    from multiprocessing import shared_memory
+
     import numpy as np
-    import torch
+
+    arr = np.ascontiguousarray(arr)
+    shm = shared_memory.SharedMemory(create=True, size=max(1, arr.nbytes))
+    np.ndarray(arr.shape, arr.dtype, buffer=shm.buf)[...] = arr
+    keep.append(shm)
+    return (shm.name, arr.shape, arr.dtype.str)
+
+
+_ATTACHED = {}
+
+
+def _shm_get(desc):
+    from multiprocessing import shared_memory
+
+    import numpy as np
+
+    name, shape, dt = desc
+    if name not in _ATTACHED:
+        _ATTACHED[name] = shared_memory.SharedMemory(name=name)
+    return np.ndarray(shape, np.dtype(dt), buffer=_ATTACHED[name].buf)
+
+
+def _shm_release():
+    for shm in _ATTACHED.values():
+        shm.close()
+    _ATTACHED.clear()
+
+
+def _ref_warm(_):
+    from oracle import pasa_oracle  # noqa: F401
+
+    return os.getpid()
+
+
+def _ref_stats(task):
+    """Block statistics and group means of whole groups [g0, g1) (oracle)."""
+    from oracle import pasa_oracle as O
+
+    qd, kd, vd, T, g0, g1, dt = task
+    t0, t1 = g0 * 2048, min(T, g1 * 2048)
+    q, k, v = (_shm_get(d)[None, t0:t1] for d in (qd, kd, vd))
+    qc, kc, vc, hc, hn = O.chunk_reduce(q, k, v, 64, dt)
+    hg = O.group_mean(hc, 32, dt)
+    _shm_release()
+    return g0, qc[0], kc[0], vc[0], hn[0], hg[0]
+
+
+def _ref_select(task):
+    from oracle import pasa_oracle as O
+
+    qcd, kcd, hnd, i0, i1, scale, NS, dt = task
+    qc, kc, hn = _shm_get(qcd), _shm_get(kcd), _shm_get(hnd)
+    idx, _ = O.select_blocks(qc[None, i0:i1], kc[None], hn[None], scale, NS, dt)
+    _shm_release()
+    return i0, idx[0]
+
+
+def _ref_attn(task):
+    import numpy as np
 
     from oracle import pasa_oracle as O
+
+    qd, kd, vd, kcd, vcd, hgd, idxd, scale, T, qb, dt = task
+    arrs = [_shm_get(d)[None] for d in (qd, kd, vd, kcd, vcd, hgd, idxd)]
+    o = O.attention(*arrs, scale, T, dtype=dt, qblocks=np.asarray(qb))
+    _shm_release()
+    return float(np.abs(o).sum())
+
+
+class OracleHead:
+    """One head of the PASA forward on the oracle, split over a pool of
+    single-threaded worker processes (spawned, so it is safe next to CUDA):
+    block statistics by group ranges, selection by query-block ranges,
+    attention by query-block ranges.  Each piece computes what the whole-head
+    oracle computes for its blocks."""
+
+    def __init__(self, workers=None):
+        import multiprocessing as mp
+
+        self.workers = workers or len(os.sched_getaffinity(0))
+        for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = "1"  # one thread per worker process
+        self.pool = mp.get_context("spawn").Pool(self.workers)
+        self.pool.map(_ref_warm, range(self.workers))  # worker start-up and imports stay out of the timing
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+    def run(self, q, k, v, w):
+        """q, k, v: one head as float32 [T, D] arrays holding the workload's
+        values.  Returns (seconds, checksum)."""
+        import numpy as np
+
+        dt = "bf16" if w.dtype_name == "bf16" else "fp32"
+        keep = []
+        try:
+            # zero rows past T up to whole blocks, so the workers' block views
+            # of q, k, v need no copy (the oracle masks by T itself)
+            pad = w.NT * 64 - w.T
+            qd, kd, vd = (_shm_put(np.concatenate([x, np.zeros((pad, x.shape[1]), np.float32)]) if pad else x, keep)
+                          for x in (q, k, v))
+            t0 = time.perf_counter()
+            NG = w.NG
+            n = self.workers
+            ranges = np.array_split(np.arange(NG), min(NG, 4 * n))
+            res = self.pool.map(_ref_stats, [(qd, kd, vd, w.T, int(r[0]), int(r[-1]) + 1, dt)
+                                             for r in ranges if len(r)])
+            res.sort(key=lambda x: x[0])
+            qc, kc, vc, hn, hg = (np.concatenate([x[i] for x in res]) for i in range(1, 6))
+            qcd, kcd, vcd, hnd, hgd = (_shm_put(x, keep) for x in (qc, kc, vc, hn, hg))
+            rows = np.array_split(np.arange(w.NT), min(w.NT, 4 * n))
+            sel = self.pool.map(_ref_select, [(qcd, kcd, hnd, int(r[0]), int(r[-1]) + 1, w.D ** -0.5, w.NS, dt)
+                                              for r in rows if len(r)])
+            sel.sort(key=lambda x: x[0])
+            idx = np.concatenate([x[1] for x in sel]).astype(np.int32)
+            idxd = _shm_put(idx, keep)
+            qbs = np.array_split(np.arange(w.NT), min(w.NT, 4 * n))
+            sums = self.pool.map(_ref_attn, [(qd, kd, vd, kcd, vcd, hgd, idxd, w.D ** -0.5, w.T, r.tolist(), dt)
+                                             for r in qbs if len(r)])
+            return time.perf_counter() - t0, float(sum(sums))
+        finally:
+            for shm in keep:
+                shm.close()
+                shm.unlink()
+
+
+def _head_arrays(w, head, seed=0):
+    import torch
+
     from pasa_b200 import synth
 
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        threads = 1
     torch.set_num_threads(os.cpu_count() or 1)
-    q, k, v = synth.head_qkv(w, 0, "cpu", seed)
-    dt = "bf16" if w.dtype == torch.bfloat16 else "fp32"
-    qf, kf, vf = (t.float().numpy()[None] for t in (q, k, v))
-    t0 = time.perf_counter()
-    qc, kc, vc, hc, hn = O.chunk_reduce(qf, kf, vf, 64, dt)
-    hg = O.group_mean(hc, 32, dt)
-    idx, _ = O.select_blocks(qc, kc, hn, w.D ** -0.5, w.NS, dt)
-    t_stats = time.perf_counter() - t0
+    q, k, v = synth.head_qkv(w, head, "cpu", seed)
+    return tuple(t.float().numpy() for t in (q, k, v))
 
-    def attn(nq):
-        sel = np.linspace(0, w.NT - 1, nq).astype(np.int64)
-        t1 = time.perf_counter()
-        O.attention(qf, kf, vf, kc, vc, hg, idx, w.D ** -0.5, w.T, dtype=dt, qblocks=sel)
-        return time.perf_counter() - t1
 
-    probe = min(4, w.NT)
-    per_block = attn(probe) / probe
-    nq = int(max(probe, min(w.NT, (target_s - t_stats) / max(per_block, 1e-6))))
-    t_attn = attn(nq)
-    per_head = t_stats + t_attn * (w.NT / nq)
-    total_s = per_head * w.heads
-    value = w.exact_flops() / total_s / 1e12
-    sample = (f"oracle (numpy) on head 0 of {w.name}: block statistics + selection for all {w.NT} blocks "
-              f"({t_stats:.1f}s) and attention for {nq} of {w.NT} query blocks ({t_attn:.1f}s), extrapolated "
-              f"x{w.NT / nq:.1f} blocks and x{w.heads} heads -> {total_s:.0f} s/call")
-    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
-            "s_per_call": total_s}
+def cpu_baseline(w, seed=0, oracle=None):
+    """The oracle on head 0 of the workload (all blocks: statistics,
+    selection and attention) over all host cores; extrapolated x heads."""
+    own = oracle is None
+    oracle = oracle or OracleHead()
+    try:
+        secs, _ = oracle.run(*_head_arrays(w, 0, seed), w)
+    finally:
+        if own:
+            oracle.close()
+    value = w.exact_flops(1) / secs / 1e12
+    sample = (f"oracle (numpy restatement) on head 0 of {w.name}, all {w.NT} blocks: statistics, selection and "
+              f"attention, {secs:.2f} s on {oracle.workers} single-threaded worker processes; the call has "
+              f"{w.heads} such heads ({secs * w.heads:.0f} s extrapolated)")
+    return {"value": value, "unit": UNIT, "cores": oracle.workers, "kind": "port", "sample": sample,
+            "cpu_model": cpu_model(), "s_per_head": secs}
 
 
 # ---------------------------------------------------------------------------
@@ -205,6 +329,11 @@ def barrier(world):
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU implementation of the path (the
+    oracle port; the reference's own PASA op is Python + Triton and needs a
+    GPU or the Triton interpreter) on the host cores.  One step is one full
+    head of the configured workload (heads in turn), so ms_per_step is the
+    measured time of one head; the call has w.heads of them."""
     from pasa_b200 import synth
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -212,26 +341,32 @@ def run_reference(args):
     if rank != 0:
         return
     w = synth.WORKLOADS[args.config]
-    vals = []
-    last = None
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(w, seed=0, target_s=3.0 if i < args.warmup else 12.0)
-        if i >= args.warmup:
-            vals.append(r["value"])
-            last = r
-    value = statistics.median(vals)
-    ms = w.exact_flops() / (value * 1e12) * 1e3
+    oracle = OracleHead()
+    secs = []
+    try:
+        for i in range(args.warmup + args.steps):
+            s, _ = oracle.run(*_head_arrays(w, i % w.heads), w)
+            if i >= args.warmup:
+                secs.append(s)
+    finally:
+        oracle.close()
+    sec = statistics.median(secs)
+    value = w.exact_flops(1) / sec / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if "tiny" not in args.config else "f32",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if w.dtype_name == "bf16" else "f32",
         "data": "synthetic (seeded, generated on the host)",
         "config": {"workload": w.name, "heads": w.heads, "seq_len": w.T, "head_dim": w.D, "density": w.density,
-                   "block": 64, "group": 32, "top_k": w.NS},
-        "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                   "block": 64, "group": 32, "top_k": w.NS,
+                   "step": f"one full head (all {w.NT} blocks), heads taken in turn; the call is {w.heads} heads",
+                   "ms_per_call_extrapolated": sec * 1e3 * w.heads},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.workers, "kind": "port",
+                         "cpu_model": cpu_model(),
+                         "sample": f"median of {args.steps} steps of one full head each on {oracle.workers} "
+                                   f"single-threaded worker processes (oracle port of the reference)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    line["cpu_baseline"]["value"] = value
     print(json.dumps(line), flush=True)
 
 
@@ -569,7 +704,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(w)
-        cpu.pop("s_per_call", None)
+        cpu.pop("s_per_head", None)
 
     if rank == 0:
         line = {

@@ -26,6 +26,10 @@ class Workload:
     text_tokens: int = 0
 
     @property
+    def dtype_name(self) -> str:
+        return "bf16" if self.dtype == torch.bfloat16 else "fp32"
+
+    @property
     def NT(self) -> int:
         return -(-self.T // 64)
 
