@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tcgen05", "simt"])
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads (small profiling cases)")
+    ap.add_argument("--place", action="store_true",
+                    help="time the HunyuanVideo token placement (forward on q, k, v and inverse on o) at the "
+                         "hunyuan-720p shape")
     ap.add_argument("--dit", action="store_true",
                     help="time the full Wan2.1-14B DiT denoising step (PASA in every layer, Ulysses over ranks)")
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks in the DiT step (40 = the full model)")
@@ -310,6 +313,10 @@ def init_dist():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        # host buffers of this rank on its GPU's NUMA node (end-to-end copies)
+        from pasa_b200 import dist as pdist
+
+        os.environ["PASA_NUMA_NODE"] = str(pdist.pin_to_gpu_numa(local))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
@@ -543,8 +550,72 @@ def run_dit(args):
         dist.destroy_process_group()
 
 
+def run_place(args):
+    """The token placement of the HunyuanVideo processors (placement.py) at
+    the hunyuan-720p shape: frame-major -> token-major on q, k and v, and the
+    inverse on the attention output, for half of the 24 heads temporal.  A
+    pure copy: the roofline is HBM bandwidth, 2 x the bytes moved."""
+    import torch
+
+    from pasa_b200 import ops, synth
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's placement kernels are Triton GPU "
+                          "kernels (placement.py), which cannot run here; its CPU form is the torch reordering the "
+                          "oracle restates"}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    w = synth.WORKLOADS["hunyuan-720p"]
+    H, T, D = w.heads, w.T, w.D
+    ctx, F, S = w.text_tokens, w.frames, w.frame_tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q, k, v = (torch.randn((1, H, T, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    qo, ko, vo, back = (torch.empty_like(q) for _ in range(4))
+    best = (torch.arange(H, device=dev) % 2).reshape(1, H)  # every other head temporal
+
+    def step():
+        ops.hunyuan_sparse_head_placement(q, k, v, qo, ko, vo, best, ctx, F, S)
+        ops.hunyuan_hidden_states_placement(vo, back, best, ctx, F, S)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert torch.equal(back, v), "inverse placement does not restore the input"
+    stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler([0])
+    with sampler:
+        time.sleep(0.2)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = 4 * q.numel() * q.element_size() * 2  # 4 tensors, read + write
+    peaks, kind = load_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "HunyuanVideo token placement, GB/s moved (forward on q, k, v + inverse on o)",
+        "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "hunyuan-720p placement", "heads": H, "seq_len": T, "head_dim": D,
+                   "context_length": ctx, "num_frame": F, "frame_size": S, "temporal_heads": H // 2,
+                   "l2": "4 x 0.73 GB tensors > 126 MB L2; no flush"},
+        "roofline": {"kernel": "place_kernel", "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                     "peak_source": f"{kind} hbm_gbs"},
+        "clocks": sampler.summary(), "gpu_launches": 4 * args.steps,
+    }), flush=True)
+
+
 def main():
     args = parse()
+    if args.place:
+        run_place(args)
+        return
     if args.dit:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference's DiT step needs diffusers and "
@@ -567,7 +638,18 @@ def main():
         import dataclasses
 
         w = dataclasses.replace(w, heads=args.heads)
-    heads = synth.shard_heads(w.heads, rank, world)
+    # heads split over the ranks when the world size divides them; otherwise
+    # (12 heads over 8 GPUs, say) ranges of query blocks, each rank preparing
+    # the heads its range touches (pasa_forward_range)
+    block_mode = world > 1 and w.heads % world != 0
+    if block_mode:
+        blk_b, blk_e = synth.shard_blocks(w.heads, w.NT, rank, world)
+        heads = range(blk_b // w.NT, -(-blk_e // w.NT))
+        blk_b, blk_e = blk_b - heads.start * w.NT, blk_e - heads.start * w.NT  # within the rank's heads
+        units = (blk_e - blk_b) / w.NT  # heads' worth of query blocks
+    else:
+        heads = synth.shard_heads(w.heads, rank, world)
+        units = len(heads)
     nh = len(heads)
     kernel = {"auto": _lib.ATTN_AUTO, "tcgen05": _lib.ATTN_TCGEN05, "simt": _lib.ATTN_SIMT}[args.kernel]
 
@@ -581,6 +663,13 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     def step(ev=None):
+        if block_mode:  # one call: prep and selection of the touched heads, attention on the range
+            if ev: ev[0].record(stream)
+            if ev: ev[1].record(stream)
+            if ev: ev[2].record(stream)
+            ops.pisa_pg_attention_range(q, k, v, blk_b, blk_e, density=w.density, out=o)
+            if ev: ev[3].record(stream)
+            return
         if ev: ev[0].record(stream)
         ops.prep(q, k, v, st)
         if ev: ev[1].record(stream)
@@ -630,8 +719,16 @@ def main():
     if not args.no_e2e:
         qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
         oh = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+        rows = slice(blk_b * 64, min(blk_e * 64, H * T)) if block_mode else None
 
         def e2e_step():
+            if block_mode:
+                # the touched heads in, the rank's rows out (no chunk pipeline)
+                for hd, dd in ((qh, q), (kh, k), (vh, v)):
+                    dd.copy_(hd, non_blocking=True)
+                ops.pisa_pg_attention_range(q, k, v, blk_b, blk_e, density=w.density, out=o)
+                oh.view(H * T, D)[rows].copy_(o.view(H * T, D)[rows], non_blocking=True)
+                return
             # host buffers in, host buffer out: the copies of head chunk i+1 (in)
             # and i-1 (out) overlap the GPU work on chunk i (pasa_forward_host)
             ops.pisa_pg_attention_host(qh, kh, vh, density=w.density, heads_per_chunk=args.e2e_chunk, out=oh,
@@ -652,31 +749,37 @@ def main():
         # every step's result is read back: check it once (cheap) after timing
         assert torch.isfinite(oh.float()).all()
         nbytes = lambda t: t.numel() * t.element_size()
+        h2d = max_over_ranks(nbytes(q) + nbytes(k) + nbytes(v), world) * world
+        d2h = (rows.stop - rows.start) * D * o.element_size() if block_mode else nbytes(o)
         e2e = {"value": F / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": nbytes(q) + nbytes(k) + nbytes(v), "d2h_bytes_per_step": nbytes(o),
-               "heads_per_chunk": args.e2e_chunk,
-               "note": ("per rank, summed over ranks; " if world > 1 else "")
-               + "pisa_pg_attention_host: pinned host q/k/v in, pinned host o out, copies pipelined over head chunks"}
-        if world > 1:
-            e2e["h2d_bytes_per_step"] *= world
-            e2e["d2h_bytes_per_step"] *= world
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": max_over_ranks(d2h, world) * world,
+               "heads_per_chunk": None if block_mode else args.e2e_chunk,
+               "h2d_gbs_per_rank": (nbytes(q) + nbytes(k) + nbytes(v)) / (e2e_ms * 1e-3) / 1e9,
+               "numa_node": int(os.environ.get("PASA_NUMA_NODE", "-1")),
+               "note": ("per rank (the largest), times the ranks; " if world > 1 else "")
+               + ("pinned host q/k/v of the rank's heads in, the rank's rows of o out, pisa_pg_attention_range"
+                  if block_mode else "pisa_pg_attention_host: pinned host q/k/v in, pinned host o out, copies "
+                  "pipelined over head chunks")}
 
     peaks, peak_kind = load_peaks()
-    peak_tf = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
-    F_rank = w.exact_flops(nh)
+    # the attention kernel runs inside a call of ~25 ms, so the burst figure
+    # is its denominator; the sustained one is reported beside it
+    peak_tf = peaks.get("bf16_tflops") or peaks.get("bf16_tflops_sustained")
+    peak_sus = peaks.get("bf16_tflops_sustained") or peak_tf
+    F_rank = w.exact_flops(units)
     achieved = F_rank / (attn_ms * 1e-3) / 1e12
     resolved = kernel if kernel != _lib.ATTN_AUTO else (
         _lib.ATTN_TCGEN05 if q.dtype == torch.bfloat16 else _lib.ATTN_SIMT)  # as pasa_attn resolves AUTO
     traffic = ATTN_TRAFFIC_BYTES.get((w.name, "tcgen05" if resolved == _lib.ATTN_TCGEN05 else "simt"))
     if traffic is not None:
         full = synth.WORKLOADS[args.config].heads
-        traffic = traffic * nh / full  # this rank's launch covers nh of the workload's heads
+        traffic = traffic * units / full  # this rank's launch covers `units` of the workload's heads
     # MMA work the tensor-core kernel executes on this call's selections: a CTA
     # serves query blocks 2p and 2p+1 and takes ceil(|S_2p ∪ S_2p+1| / 2)
     # steps of two key blocks (score and P.V MMAs, M=128, N=K=128), then one
     # step per 32-block group (scores N=32, P_g.vc_g K=32, U.H_g K=D)
     exec_flop = None
-    if resolved == _lib.ATTN_TCGEN05:
+    if resolved == _lib.ATTN_TCGEN05 and not block_mode:
         m = st.sel_mask.view(torch.int32)
         a, b = m[:, 0::2], m[:, 1::2]
         if b.shape[1] < a.shape[1]:
@@ -690,9 +793,12 @@ def main():
         "kernel": f"attn_tc_kernel<{D}>" if resolved == _lib.ATTN_TCGEN05 else f"attn_simt_kernel<{D}>",
         "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
         "frac": achieved / peak_tf, "traffic": traffic,
-        "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
-        "achieved_basis": "exact-block FLOPs per launch / mean CUDA-event launch time",
-        "achieved_incl_correction": (w.exact_flops(nh) + w.corr_flops(nh)) / (attn_ms * 1e-3) / 1e12,
+        "peak_source": f"{peak_kind} bf16_tflops (burst: the kernel runs inside a ~25 ms call)",
+        "peak_sustained": peak_sus, "frac_sustained": achieved / peak_sus,
+        "achieved_basis": ("exact-block FLOPs per launch / mean CUDA-event launch time" if not block_mode else
+                           "exact-block FLOPs of the rank's blocks / whole pasa_forward_range call (prep and "
+                           "selection included)"),
+        "achieved_incl_correction": (w.exact_flops(units) + w.corr_flops(units)) / (attn_ms * 1e-3) / 1e12,
     }
     if exec_flop is not None:
         # the MMAs the kernel runs (union of two query blocks' selections per
@@ -700,6 +806,7 @@ def main():
         roofline["executed_tflop"] = exec_flop / 1e12
         roofline["achieved_executed"] = exec_flop / (attn_ms * 1e-3) / 1e12
         roofline["frac_executed"] = roofline["achieved_executed"] / peak_tf
+        roofline["frac_executed_sustained"] = roofline["achieved_executed"] / peak_sus
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -713,10 +820,13 @@ def main():
             "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32",
             "data": "synthetic (seeded N(0,1), AR(1) keys across frames; generated on the device)",
             "config": {"workload": w.name, "heads": w.heads, "seq_len": T, "head_dim": D, "density": w.density,
-                       "block": 64, "group": 32, "top_k": NS, "parallelism": f"heads/{world}",
+                       "block": 64, "group": 32, "top_k": NS,
+                       "parallelism": (f"query-block ranges/{world} (heads do not divide)" if block_mode
+                                       else f"heads/{world}"),
                        "l2": "inputs 2.3 GB per call > 126 MB L2; no flush" if w.name == "wan14b-720p" else
                        "see workload size"},
-            "kernels_ms": {"prep": prep_ms, "select": sel_ms, "attn": attn_ms},
+            "kernels_ms": ({"forward_range": attn_ms} if block_mode else
+                           {"prep": prep_ms, "select": sel_ms, "attn": attn_ms}),
             "exact_tflop": F / 1e12, "corr_tflop": Fc / 1e12,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
             "gpu_launches": 3 * args.steps,

@@ -151,6 +151,26 @@ PASA_API int pasa_forward(void* stream, const void* q, const void* k, const void
                  double density, float scale, int use_cov_bias, const float* noise,
                  void* workspace, size_t workspace_bytes, void* o, int kernel);
 
+/*
+ * pasa_forward restricted to a range of query blocks, for callers that
+ * split one call over several GPUs finer than by heads (12 heads over 8
+ * GPUs, say).  No counterpart in the reference, which runs the whole op on
+ * one device.  The B*H*NT query blocks are numbered head by head
+ * (bh * NT + block); [block_begin, block_end) selects some of them.  The
+ * heads they touch are prepared and selected whole (a head shared with
+ * another range is prepared by both), and only the rows of the selected
+ * blocks of o ([B*H, T, D], bf16, tensor-core kernel) are written; every
+ * other row of o is left as it was.  The union of disjoint ranges that
+ * cover all blocks gives pasa_forward's output bit for bit.
+ *   workspace: pasa_forward_range_workspace_size() bytes (256-byte aligned)
+ */
+PASA_API int pasa_forward_range_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype,
+                 double density, int64_t block_begin, int64_t block_end, size_t* bytes);
+PASA_API int pasa_forward_range(void* stream, const void* q, const void* k, const void* v,
+                 int64_t B, int64_t H, int64_t T, int D, int dtype, double density, float scale,
+                 int use_cov_bias, const float* noise, void* workspace, size_t workspace_bytes,
+                 void* o, int kernel, int64_t block_begin, int64_t block_end);
+
 /* Output layouts of pasa_forward_ex. */
 typedef enum pasa_o_layout {
   PASA_O_BHTD = 0,  /* o [B*H, T, D] (head-major), as pasa_forward           */
@@ -270,6 +290,7 @@ PASA_API int pasa_sample_mse(void* stream, const void* q, const void* k, const v
  *   src, dst          [cfg, H, T, D], T = context_length + num_frame*frame_size
  *   head_is_temporal  [cfg, H] int32 (the best_mask_idx of the reference)
  * Spatial heads (0) are copied unchanged.  src and dst must not overlap.
+ * Rows of D elements are 16-byte multiples of at most 4096 bytes.
  */
 PASA_API int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_temporal,
                int64_t cfg, int64_t H, int64_t T, int D, int dtype,

@@ -12,12 +12,14 @@ from .ops import (  # noqa: F401
     piecewise_sparse_attention,
     pisa_pg_attention,
     pisa_pg_attention_host,
+    pisa_pg_attention_range,
 )
 
 __all__ = [
     "dense_attention",
     "pisa_pg_attention",
     "pisa_pg_attention_host",
+    "pisa_pg_attention_range",
     "piecewise_sparse_attention",
     "hunyuan_sparse_head_placement",
     "hunyuan_hidden_states_placement",

@@ -47,7 +47,8 @@ EXPORTS = (
     "pasa_forward_host_workspace_size", "pasa_forward_host", "pasa_dense_attn",
     "pasa_dit_row_norm", "pasa_dit_qkv_rope", "pasa_forward_ex", "pasa_peer_alloc", "pasa_peer_free",
     "pasa_peer_open", "pasa_peer_close", "pasa_dit_qkv_rope_scatter", "pasa_forward_scatter",
-    "pasa_sample_mse_workspace_size", "pasa_sample_mse",
+    "pasa_sample_mse_workspace_size", "pasa_sample_mse", "pasa_forward_range_workspace_size",
+    "pasa_forward_range",
 )
 
 _lib = None
@@ -98,6 +99,10 @@ def load() -> ctypes.CDLL:
         "pasa_sample_mse_workspace_size": (c_int, [c_int64, c_int64, c_int, POINTER(c_size_t)]),
         "pasa_sample_mse": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, P, c_int64, c_int,
                                     c_int64, c_int64, c_int64, P, c_size_t, P, P]),
+        "pasa_forward_range_workspace_size": (c_int, [c_int64, c_int64, c_int64, c_int, c_int, c_double, c_int64,
+                                                      c_int64, POINTER(c_size_t)]),
+        "pasa_forward_range": (c_int, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_double, c_float,
+                                       c_int, P, P, c_size_t, P, c_int, c_int64, c_int64]),
         "pasa_dit_row_norm": (c_int, [P, P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_float, c_int, P]),
         "pasa_dit_qkv_rope": (c_int, [P, P, P, P, P, P, P, P, c_int64, c_int64, c_int, c_int, c_float, c_int,
                                       P, P, P]),

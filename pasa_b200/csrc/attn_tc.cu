@@ -146,6 +146,9 @@ struct Params {
   __nv_bfloat16* const* o_peer;
   int o_npeer;
   int64_t o_tokens, o_heads_total, o_head0;
+  // CTA p works on the query-block pair pair0 + p and stores only the rows
+  // of query blocks in [blk_lo, blk_hi) (a block range of the head)
+  int64_t pair0, blk_lo, blk_hi;
 };
 
 // Optional step tracer (compile with -DPASA_TRACE): one CTA, chosen with
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   if (tid == 0) PASA_TRACE_CTL(0);
   const unsigned long long pasa_t0_ns = global_ns(), pasa_t0_clk = clock64();
 #endif
-  const int64_t pair = blockIdx.x, bh = blockIdx.y;
+  const int64_t pair = blockIdx.x + P.pair0, bh = blockIdx.y;
   const int64_t NT = P.NT, NG = P.NG;
   const int64_t blkA = 2 * pair, blkB = 2 * pair + 1;
   const bool hasB = blkB < NT;
@@ -774,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       const float l_tot = row_reduce(l1, false);
       const float g_tot = row_reduce(gl, false);
       if (wok) {  // warp-uniform: tcgen05.ld is warp-collective
-        const bool store = t < P.T;
+        const bool store = t < P.T && blk >= P.blk_lo && blk < P.blk_hi;
         const float denom = l_tot + g_tot * fast_exp2(m_true - m_used);
         const float inv = 1.0f / denom;
         __nv_bfloat16* orow;
@@ -866,7 +869,7 @@ template <int D>
 cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const void* v, const void* kc,
                         const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
                         float scale, void* o, uint32_t* err, int dense, int64_t o_heads,
-                        const OutScatter& sc) {
+                        const OutScatter& sc, int64_t blk_lo, int64_t blk_hi) {
   using C = Cfg<D>;
   const int64_t NT = cdiv(T_len, kBlock), NG = cdiv(NT, kGroup), NTP = NG * kGroup;
   if (NT > kMaxNT) return cudaErrorInvalidValue;
@@ -884,10 +887,17 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
   p.o_tokens = sc.tokens;
   p.o_heads_total = sc.heads_total;
   p.o_head0 = sc.head0;
+  // the pairs that hold blocks [blk_lo, blk_hi)
+  if (blk_hi < 0) blk_hi = NT;
+  if (blk_lo < 0 || blk_lo >= blk_hi || blk_hi > NT) return cudaErrorInvalidValue;
+  p.pair0 = blk_lo / 2;
+  p.blk_lo = blk_lo;
+  p.blk_hi = blk_hi;
+  const int64_t npairs = cdiv(blk_hi, 2) - p.pair0;
   auto kern = attn_tc_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid{unsigned(cdiv(NT, 2)), unsigned(BH), 1u};
+  dim3 grid{unsigned(npairs), unsigned(BH), 1u};
   kern<<<grid, kThreads, C::kSmemBytes, st>>>(maps, p);
   return cudaGetLastError();
 }
@@ -897,10 +907,12 @@ cudaError_t launch_tc_t(cudaStream_t st, const void* q, const void* k, const voi
 cudaError_t launch_attn_tc(cudaStream_t st, int D, const void* q, const void* k, const void* v, const void* kc,
                            const void* vc, const void* hg, const uint32_t* mask, int64_t BH, int64_t T_len,
                            int64_t /*NS*/, float scale, void* o, uint32_t* err, int dense, int64_t o_heads,
-                           const OutScatter& sc) {
+                           const OutScatter& sc, int64_t blk_lo, int64_t blk_hi) {
   if (D == 64)
-    return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads, sc);
-  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads, sc);
+    return tc::launch_tc_t<64>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads, sc, blk_lo,
+                               blk_hi);
+  return tc::launch_tc_t<128>(st, q, k, v, kc, vc, hg, mask, BH, T_len, scale, o, err, dense, o_heads, sc, blk_lo,
+                              blk_hi);
 }
 
 }  // namespace pasa

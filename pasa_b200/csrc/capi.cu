@@ -17,7 +17,7 @@ cudaError_t launch_attn_simt(cudaStream_t, int, int, const void*, const void*, c
                              int64_t, float, void*);
 cudaError_t launch_attn_tc(cudaStream_t, int, const void*, const void*, const void*, const void*, const void*,
                            const void*, const uint32_t*, int64_t, int64_t, int64_t, float, void*, uint32_t*, int,
-                           int64_t, const OutScatter&);
+                           int64_t, const OutScatter&, int64_t blk_lo, int64_t blk_hi);
 cudaError_t launch_place(cudaStream_t, const void*, void*, const int32_t*, int64_t, int64_t, int64_t, int, int,
                          int64_t, int64_t, int64_t, int);
 size_t sample_mse_workspace(int64_t BH, int64_t T, int D);
@@ -186,7 +186,7 @@ int attn_dispatch(void* stream, const void* q, const void* k, const void* v, con
   if (kernel == PASA_ATTN_TCGEN05) {
     if (dtype != PASA_BF16) return PASA_ERR_DTYPE;
     return cuda_status(launch_attn_tc(s, D, q, k, v, kc, vc, h_group, sel_mask, BH, T, ns, scale, o, err_word, 0,
-                                      o_heads, sc));
+                                      o_heads, sc, 0, -1));
   }
   if (kernel != PASA_ATTN_SIMT) return PASA_ERR_UNSUPPORTED;
   if (o_heads > 0 || scatter) return PASA_ERR_UNSUPPORTED;  // the CUDA-core kernel writes [B*H, T, D] only
@@ -277,6 +277,95 @@ int pasa_forward_scatter(void* stream, const void* q, const void* k, const void*
                       workspace_bytes, nullptr, PASA_ATTN_TCGEN05, 0, sc);
 }
 
+namespace {
+
+// heads [h0, h1) that hold the query blocks [block_begin, block_end) of the
+// B*H*NT blocks in (head, block) order
+int range_heads(int64_t B, int64_t H, int64_t T, int64_t block_begin, int64_t block_end, int64_t* h0,
+                int64_t* h1) {
+  const int64_t NT = cdiv(T, kBlock);
+  if (block_begin < 0 || block_end <= block_begin || block_end > B * H * NT) return PASA_ERR_SHAPE;
+  *h0 = block_begin / NT;
+  *h1 = cdiv(block_end, NT);
+  return PASA_OK;
+}
+
+}  // namespace
+
+int pasa_forward_range_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype, double density,
+                                      int64_t block_begin, int64_t block_end, size_t* bytes) {
+  if (!bytes) return PASA_ERR_NULL;
+  if (B < 1 || H < 1) return PASA_ERR_SHAPE;
+  int st = check_common(B * H, T, D, dtype);
+  if (st) return st;
+  if (!std::isfinite(density)) return PASA_ERR_DENSITY;
+  int64_t h0 = 0, h1 = 0;
+  if ((st = range_heads(B, H, T, block_begin, block_end, &h0, &h1))) return st;
+  *bytes = make_layout(h1 - h0, T, D, esize_of(dtype), top_k_of(density, cdiv(T, kBlock))).total;
+  return PASA_OK;
+}
+
+int pasa_forward_range(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T,
+                       int D, int dtype, double density, float scale, int use_cov_bias, const float* noise,
+                       void* workspace, size_t workspace_bytes, void* o, int kernel, int64_t block_begin,
+                       int64_t block_end) {
+  if (B < 1 || H < 1) return PASA_ERR_SHAPE;
+  int st = check_common(B * H, T, D, dtype);
+  if (st) return st;
+  if (!std::isfinite(density)) return PASA_ERR_DENSITY;
+  if (kernel != PASA_ATTN_AUTO && kernel != PASA_ATTN_TCGEN05) return PASA_ERR_UNSUPPORTED;
+  if (dtype != PASA_BF16) return PASA_ERR_DTYPE;  // the tensor-core kernel runs bf16
+  if (!q || !k || !v || !o) return PASA_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return PASA_ERR_ALIGN;
+  if (!std::isfinite(scale)) return PASA_ERR_SHAPE;
+  int64_t h0 = 0, h1 = 0;
+  if ((st = range_heads(B, H, T, block_begin, block_end, &h0, &h1))) return st;
+  const int64_t NT = cdiv(T, kBlock), NS = top_k_of(density, NT), BHt = h1 - h0;
+  const Layout L = make_layout(BHt, T, D, esize_of(dtype), NS);
+  if (!workspace || workspace_bytes < L.total) return PASA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PASA_ERR_ALIGN;
+  if ((st = check_select_fit(D, NT, NS))) return st;
+  if ((st = check_device())) return st;
+  const size_t head_bytes = size_t(T) * D * esize_of(dtype);
+  auto at = [&](const void* base, int64_t h) { return static_cast<const char*>(base) + size_t(h) * head_bytes; };
+  char* w = static_cast<char*>(workspace);
+  char* qc = w + L.off_qc;
+  char* kc = w + L.off_kc;
+  char* vc = w + L.off_vc;
+  float* hn = reinterpret_cast<float*>(w + L.off_hnorm);
+  char* hg = w + L.off_hgroup;
+  int32_t* idx = reinterpret_cast<int32_t*>(w + L.off_idx);
+  uint32_t* mask = reinterpret_cast<uint32_t*>(w + L.off_mask);
+  uint32_t* err = reinterpret_cast<uint32_t*>(w + L.off_err);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the block statistics and the selection cover the touched heads whole
+  // (a head shared with another caller's range is prepared by both)
+  if ((st = pasa_prep(stream, at(q, h0), at(k, h0), at(v, h0), 1, BHt, T, D, dtype, kBlock, kGroup, qc, kc, vc, hn,
+                      hg)))
+    return st;
+  if ((st = pasa_select(stream, qc, kc, hn, noise ? noise + h0 * NT : nullptr, BHt, NT, D, dtype, scale,
+                        use_cov_bias, NS, idx, mask)))
+    return st;
+  if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
+  const size_t stat_bytes = size_t(L.NTP) * D * esize_of(dtype), hg_bytes = size_t(L.NG) * D * D * esize_of(dtype);
+  // attention: the first and the last head may be partial, the heads between are whole
+  int64_t h = h0;
+  while (h < h1) {
+    const int64_t lo = (h == h0) ? block_begin - h0 * NT : 0;
+    const int64_t hi = (h == h1 - 1) ? block_end - (h1 - 1) * NT : NT;
+    int64_t n = 1;  // whole heads go in one launch
+    if (lo == 0 && hi == NT)
+      while (h + n < h1 && !(h + n == h1 - 1 && block_end - (h1 - 1) * NT != NT)) ++n;
+    const int64_t j = h - h0;
+    cudaError_t e = launch_attn_tc(s, D, at(q, h), at(k, h), at(v, h), kc + j * stat_bytes, vc + j * stat_bytes,
+                                   hg + j * hg_bytes, mask + j * NT * L.NG, n, T, NS, scale,
+                                   static_cast<char*>(o) + size_t(h) * head_bytes, err, 0, 0, OutScatter{}, lo, hi);
+    if (e != cudaSuccess) return PASA_ERR_CUDA;
+    h += n;
+  }
+  return PASA_OK;
+}
+
 int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, int64_t BH, int64_t T, int D,
                     int dtype, float scale, void* o, uint32_t* err_word) {
   int st = check_common(BH, T, D, dtype);
@@ -288,7 +377,7 @@ int pasa_dense_attn(void* stream, const void* q, const void* k, const void* v, i
   if ((st = check_device())) return st;
   // the block statistics are not read in dense mode; q stands in for their (unused) tensor maps
   return cuda_status(launch_attn_tc(static_cast<cudaStream_t>(stream), D, q, k, v, q, q, q, nullptr, BH, T,
-                                    cdiv(T, kBlock), scale, o, err_word, 1, 0, OutScatter{}));
+                                    cdiv(T, kBlock), scale, o, err_word, 1, 0, OutScatter{}, 0, -1));
 }
 
 int pasa_sample_mse_workspace_size(int64_t BH, int64_t T, int D, size_t* bytes) {
@@ -331,7 +420,7 @@ int pasa_place(void* stream, const void* src, void* dst, const int32_t* head_is_
                int64_t T, int D, int dtype, int64_t context_length, int64_t num_frame, int64_t frame_size,
                int inverse) {
   if (dtype != PASA_BF16 && dtype != PASA_F32) return PASA_ERR_DTYPE;
-  if (D < 8 || (D * esize_of(dtype)) % 16 != 0) return PASA_ERR_UNSUPPORTED;
+  if (D < 8 || (D * esize_of(dtype)) % 16 != 0 || D * esize_of(dtype) > 4096) return PASA_ERR_UNSUPPORTED;
   if (cfg < 1 || H < 1 || T < 1 || context_length < 0 || num_frame < 1 || frame_size < 1) return PASA_ERR_SHAPE;
   if (context_length + num_frame * frame_size != T) return PASA_ERR_SHAPE;  // placement.py:128
   if (!src || !dst || !head_is_temporal) return PASA_ERR_NULL;

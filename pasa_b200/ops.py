@@ -197,6 +197,35 @@ def pisa_pg_attention(
     return o
 
 
+def pisa_pg_attention_range(q, k, v, block_begin: int, block_end: int, density=0.15, scale=None,
+                            use_cov_bias=True, noise=None, out=None):
+    """The op on the query blocks [block_begin, block_end) of q's B*H*NT
+    blocks (numbered head by head; pasa_forward_range): only their rows of
+    ``out`` ([B, H, T, D] like v, allocated when None) are written.  For
+    splitting one call over several GPUs finer than by heads.  bf16 only
+    (tensor-core kernel).  No counterpart in the reference."""
+    _check_qkv(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, T, K = q.shape
+    scale = K ** -0.5 if scale is None else scale
+    dcode = _dtype_code(q)
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty_like(v)
+    elif out.shape != v.shape or out.dtype != v.dtype or not out.is_contiguous() or out.device != v.device:
+        raise ValueError("out must be a contiguous tensor like v")
+    with torch.cuda.device(q.device):
+        n = ctypes.c_size_t()
+        _lib.check("pasa_forward_range_workspace_size", lib.pasa_forward_range_workspace_size(
+            B, H, T, K, dcode, float(density), int(block_begin), int(block_end), ctypes.byref(n)))
+        ws = torch.empty(n.value, dtype=torch.uint8, device=q.device)
+        _lib.check("pasa_forward_range", lib.pasa_forward_range(
+            _stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, T, K, dcode, float(density),
+            float(scale), int(bool(use_cov_bias)), _ptr(noise), ws.data_ptr(), n.value, out.data_ptr(),
+            _lib.ATTN_AUTO, int(block_begin), int(block_end)))
+    return out
+
+
 def pisa_pg_attention_host(
     q, k, v,
     density=0.15,

@@ -102,3 +102,24 @@ def shard_heads(total: int, rank: int, world: int) -> range:
     base, extra = divmod(total, world)
     start = rank * base + min(rank, extra)
     return range(start, start + base + (1 if rank < extra else 0))
+
+
+def shard_blocks(heads: int, NT: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous range [begin, end) of the heads * NT query blocks (numbered
+    head by head) of one rank, for head counts the world size does not
+    divide: the ranks' block counts differ by at most three, and every
+    boundary inside a head is even, so no pair of query blocks (one tile of
+    the tensor-core kernel) is split between ranks."""
+    total = heads * NT
+
+    def cut(r):
+        if r <= 0:
+            return 0
+        if r >= world:
+            return total
+        b = (r * total) // world
+        h, j = divmod(b, NT)
+        j -= j & 1  # even within the head
+        return h * NT + j
+
+    return cut(rank), cut(rank + 1)

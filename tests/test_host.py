@@ -38,3 +38,29 @@ def test_bad_shapes_and_options_are_rejected():
         pasa_b200.pisa_pg_attention(q[0], q[0], q[0])
     with pytest.raises(ValueError):
         ops._dtype_code(torch.empty(1, dtype=torch.float16))
+
+
+def test_numa_pinning_reads_sysfs(tmp_path, monkeypatch):
+    """pin_to_gpu_numa: the GPU's PCI device's numa_node and that node's CPU
+    list, intersected with the allowed CPUs (a fake sysfs tree)."""
+    import os
+    import types
+
+    from pasa_b200 import dist as pdist
+
+    props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1b, pci_device_id=0)
+    monkeypatch.setattr(pdist.torch.cuda, "get_device_properties", lambda i: props)
+    dev = tmp_path / "bus" / "pci" / "devices" / "0000:1b:00.0"
+    dev.mkdir(parents=True)
+    (dev / "numa_node").write_text("1\n")
+    node = tmp_path / "devices" / "system" / "node" / "node1"
+    node.mkdir(parents=True)
+    allowed = sorted(os.sched_getaffinity(0))
+    (node / "cpulist").write_text(f"{allowed[0]}-{allowed[0]},{allowed[-1]}\n")
+    seen = {}
+    monkeypatch.setattr(os, "sched_setaffinity", lambda pid, cpus: seen.setdefault("cpus", set(cpus)))
+    assert pdist.gpu_numa_node(0, str(tmp_path)) == 1
+    assert pdist.pin_to_gpu_numa(0, str(tmp_path)) == 1
+    assert seen["cpus"] == {allowed[0], allowed[-1]}
+    (dev / "numa_node").write_text("-1\n")
+    assert pdist.pin_to_gpu_numa(0, str(tmp_path)) == -1

@@ -65,3 +65,19 @@ def test_shard_sizes_differ_by_at_most_one():
         for world in (1, 2, 3, 4, 8):
             sizes = [len(pdist.shard_heads(total, r, world)) for r in range(world)]
             assert sum(sizes) == total and max(sizes) - min(sizes) <= 1
+
+
+def test_block_sharding_partition():
+    """(head, query-block) shards for head counts the world size does not
+    divide: exact, disjoint, balanced within three blocks, and no pair of
+    query blocks split inside a head."""
+    for heads, NT in ((12, 512), (12, 511), (5, 37), (3, 1182)):
+        for world in (1, 2, 3, 5, 8):
+            ranges = [synth.shard_blocks(heads, NT, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == heads * NT
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+            sizes = [e - b for b, e in ranges]
+            assert min(sizes) > 0 and max(sizes) - min(sizes) <= 3
+            for b, e in ranges:
+                for x in (b, e):
+                    assert (x % NT) % 2 == 0 or x == heads * NT
