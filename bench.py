@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--place", action="store_true",
                     help="time the HunyuanVideo token placement (forward on q, k, v and inverse on o) at the "
                          "hunyuan-720p shape")
+    ap.add_argument("--classify", action="store_true",
+                    help="time the head classification (pasa_sample_mse) at the hunyuan-720p shape")
     ap.add_argument("--dit", action="store_true",
                     help="time the full Wan2.1-14B DiT denoising step (PASA in every layer, Ulysses over ranks)")
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks in the DiT step (40 = the full model)")
@@ -566,7 +568,7 @@ def run_place(args):
         return
     dev = torch.device("cuda", 0)
     w = synth.WORKLOADS["hunyuan-720p"]
-    H, T, D = w.heads, w.T, w.D
+    H, T, D = args.heads or w.heads, w.T, w.D
     ctx, F, S = w.text_tokens, w.frames, w.frame_tokens
     g = torch.Generator(device=dev)
     g.manual_seed(0)
@@ -611,10 +613,71 @@ def run_place(args):
     }), flush=True)
 
 
+def run_classify(args):
+    """Head classification (pasa_sample_mse) at the hunyuan-720p shape: 32
+    sampled rows against all 119056 keys of each of the 24 heads, three
+    masks.  HBM-bound: K is read twice and V once per head."""
+    import torch
+
+    from pasa_b200 import classify, synth
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference builds its emulated masks as dense "
+                          "T x T tensors with a Python double loop (14 GB at this shape) before sample_mse"}),
+              flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    w = synth.WORKLOADS["hunyuan-720p"]
+    H, T, D = args.heads or w.heads, w.T, w.D
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q, k, v = (torch.randn((1, H, T, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    rows = torch.randint(0, 10000, (32,), generator=torch.Generator().manual_seed(1))
+
+    def step():
+        return classify.sample_mse(q, k, v, model="hunyuan", context_length=w.text_tokens, num_frame=w.frames,
+                                   frame_size=w.frame_tokens, rows=rows)
+
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler([0])
+    with sampler:
+        time.sleep(0.2)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = 3 * H * T * D * 2  # K twice, V once
+    peaks, kind = load_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "Head classification (sampled-row MSE of the spatial/temporal masks), ms per call",
+        "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "hunyuan-720p sample_mse", "heads": H, "seq_len": T, "head_dim": D,
+                   "sampled_rows": 32, "context_length": w.text_tokens, "num_frame": w.frames,
+                   "frame_size": w.frame_tokens},
+        "roofline": {"kernel": "mse_stats_kernel + mse_pv_kernel", "bound": "hbm", "achieved": gbs,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                     "peak_source": f"{kind} hbm_gbs", "algorithmic_bytes": nbytes},
+        "clocks": sampler.summary(), "gpu_launches": 4 * args.steps,
+    }), flush=True)
+
+
 def main():
     args = parse()
     if args.place:
         run_place(args)
+        return
+    if args.classify:
+        run_classify(args)
         return
     if args.dit:
         if args.impl == "reference":

@@ -38,10 +38,28 @@ struct SelectDims {
 __device__ __forceinline__ void row_topk(const uint32_t* rk, int64_t NT, int64_t NG, int64_t NS, uint32_t* h,
                                          uint32_t* mw, uint64_t* cl, int32_t* out, uint32_t* mask_out) {
   const int lane = threadIdx.x & 31;
-  uint32_t prefix = 0, pmask = 0;
+  // The keys of a row share their high bits (the scores of a head lie in a
+  // narrow range): start the radix passes below the common prefix of the
+  // row's smallest and largest key, so the first histogram is spread over
+  // its bins instead of piling every key into one (whose shared-memory
+  // atomics serialise) and fewer passes are needed.
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+  for (int64_t j = lane; j < NT; j += 32) {
+    const uint32_t kj = rk[j];
+    kmin = kj < kmin ? kj : kmin;
+    kmax = kj > kmax ? kj : kmax;
+  }
+  kmin = __reduce_min_sync(0xffffffffu, kmin);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  const uint32_t diff = kmin ^ kmax;
+  int hi = diff ? 31 - __clz(diff) : -1;  // highest bit in which the keys differ
+  // the bits above it (all of them when every key is equal)
+  const uint32_t fixed = hi < 0 ? 0xFFFFFFFFu : (hi >= 31 ? 0u : ~((2u << hi) - 1u));
+  uint32_t prefix = kmin & fixed, pmask = fixed;
   uint32_t remaining = uint32_t(NS);
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
+  while (hi >= 0) {
+    const int shift = hi >= 7 ? hi - 7 : 0;  // digit: bits [shift, shift + 8), those above hi already fixed
+    hi = shift - 1;
     for (int b = lane; b < 256; b += 32) h[b] = 0;
     __syncwarp();
     for (int64_t j = lane; j < NT; j += 32) {
