@@ -541,7 +541,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     };
     // O holds the steps <= n-1 once their MMAs completed; one thread owns the
     // row, so it rescales all D columns
+    // A parity wait for the k-th completion of a barrier is only sound once
+    // its (k-1)-th completion has happened: with the barrier two phases
+    // behind, the parity already matches and the wait returns at once.  This
+    // set follows o_done[n & 1] step by step (its P-region waits), but not
+    // o_done[(n - 1) & 1]; so it first waits for step n-2 on its own barrier,
+    // after which step n-3 (issued earlier, completed in order) has completed
+    // too, and only then for step n-1 on the other barrier.  (Without the
+    // first wait, a rescale at step 3 could start while the P.V of step 0 was
+    // still accumulating into O, and corrupt those rows.)
     auto rescale_o = [&](int64_t n, float alpha) {
+      if (n >= 2) wait_bar(&o_done[n & 1], (n - 2) >> 1);
       if (n >= 1) { wait_bar(&o_done[(n - 1) & 1], (n - 1) >> 1); tc_fence_after(); }
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {

@@ -15,13 +15,17 @@
 //   mse = round(mean(round(round(h_m - h_full)^2)))  torch.mean over rows, D
 // with round() the cast to the input dtype (bf16: nearest even).
 //
-// Four launches: (1) per key chunk, the masked row maxima and exponential
+// Five launches: (1) per key chunk, the masked row maxima and exponential
 // sums of the three variants (full, spatial, temporal); (2) their
 // combination per head; (3) per key chunk, the probabilities times V; (4)
-// the sum over chunks in a fixed order, the rounding of the outputs and the
-// two mean squared differences.  Every sum has a fixed order, so the result
-// is deterministic.
+// per slice of output elements, the sum over chunks in a fixed order, the
+// rounded outputs and the squared differences; (5) per head, the slices in
+// order and the two means.  Every sum has a fixed order, so the result is
+// deterministic.  bf16 inputs run the scores and the probability-times-V
+// products on the tensor cores (mma.sync m16n8k16, bf16 x bf16 -> fp32,
+// the reference matmuls' arithmetic); fp32 inputs on CUDA cores.
 #include <cmath>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -65,6 +69,36 @@ __device__ __forceinline__ bool allowed(int var, int64_t q, int64_t k, const Spe
 
 template <typename T>
 __device__ __forceinline__ float rnd(float x) { return Elem<T>::round(x); }
+
+// The mask-relevant facts of one position, computed once per row or key
+// (the token-major index needs a division by the frame size): the same
+// predicate as allowed(), split in two halves.
+struct Pos {
+  int32_t b_sp, b_tm;     // 128-token block in frame-major and in token-major order
+  bool sink_sp, sink_tm;  // inside the first frame (Wan's sink), in either order
+  bool text;              // a HunyuanVideo text token (attends and is attended by all)
+};
+
+__device__ __forceinline__ Pos pos_of(int64_t x, const Spec& m) {
+  Pos p;
+  const int64_t xc = x < m.V ? x : m.V - 1;
+  const int64_t tm = token_major(xc, m);
+  p.b_sp = int32_t(x / 128);
+  p.b_tm = int32_t(tm / 128);
+  p.sink_sp = x < m.S;
+  p.sink_tm = tm < m.S;
+  p.text = (m.model == 0) && x >= m.V;
+  return p;
+}
+
+__device__ __forceinline__ bool allowed_pos(int var, const Pos& q, const Pos& k, const Spec& m) {
+  if (var == 0) return true;
+  if (m.model == 0 && (q.text || k.text)) return true;
+  const int32_t d = (var == 1) ? q.b_sp - k.b_sp : q.b_tm - k.b_tm;
+  const bool band = (d < 0 ? -d : d) < m.width;
+  if (m.model == 0) return band;
+  return band || (var == 1 ? k.sink_sp : k.sink_tm);
+}
 
 // Scores of this thread's 4 rows x 2 keys of the tile at j0 (rows 4*warp..,
 // keys j0 + lane and j0 + lane + 32), or -inf past T.
@@ -248,15 +282,17 @@ __global__ void __launch_bounds__(kThreads) mse_pv_kernel(const T* __restrict__ 
       acc_out[(((bh * gridDim.x + c) * kVar + x) * kRows + rg * kRPT + r) * D + col] = acc[x][r];
 }
 
-// (4) per head: outputs, differences and the two mean squared differences
+// (4a) per slice of 256 output elements (row, column) of a head: the sum over
+// chunks in order, the rounded outputs of the three variants and the two
+// squared differences, summed over the slice in a fixed tree
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads) mse_finish_kernel(const float* __restrict__ acc, int64_t nchunks,
-                                                              int R, int64_t BH, T* __restrict__ mse_out,
-                                                              int32_t* __restrict__ best) {
+__global__ void __launch_bounds__(kThreads) mse_finish_part_kernel(const float* __restrict__ acc, int64_t nchunks,
+                                                                   int R, float2* __restrict__ partial) {
   __shared__ float red[2][kThreads];
-  const int64_t bh = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int e = blockIdx.x * kThreads + threadIdx.x;
   float part[2] = {0.f, 0.f};
-  for (int e = threadIdx.x; e < R * D; e += kThreads) {
+  if (e < R * D) {
     float h[kVar];
 #pragma unroll
     for (int x = 0; x < kVar; ++x) {
@@ -267,7 +303,7 @@ __global__ void __launch_bounds__(kThreads) mse_finish_kernel(const float* __res
 #pragma unroll
     for (int x = 1; x < kVar; ++x) {
       const float d = rnd<T>(h[x] - h[0]);
-      part[x - 1] += rnd<T>(d * d);
+      part[x - 1] = rnd<T>(d * d);
     }
   }
   red[0][threadIdx.x] = part[0];
@@ -280,16 +316,313 @@ __global__ void __launch_bounds__(kThreads) mse_finish_kernel(const float* __res
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) {
-    const float inv_n = 1.0f / float(R * D);
-    const float a = rnd<T>(red[0][0] * inv_n), b = rnd<T>(red[1][0] * inv_n);
-    if (mse_out) {
-      Elem<T>::store(mse_out + bh, a);       // [2, cfg*H]: spatial
-      Elem<T>::store(mse_out + BH + bh, b);  // temporal
-    }
-    if (best) best[bh] = (b < a) ? 1 : 0;    // argmin, first index on ties
+  if (threadIdx.x == 0) partial[bh * gridDim.x + blockIdx.x] = make_float2(red[0][0], red[1][0]);
+}
+
+// (4b) per head: the slices in order, the mean, the class
+template <typename T, int D>
+__global__ void mse_finish_kernel(const float2* __restrict__ partial, int nslices, int R, int64_t BH,
+                                  T* __restrict__ mse_out, int32_t* __restrict__ best) {
+  const int64_t bh = blockIdx.x;
+  if (threadIdx.x != 0) return;
+  float s0 = 0.f, s1 = 0.f;
+  for (int i = 0; i < nslices; ++i) {
+    const float2 p = partial[bh * nslices + i];
+    s0 += p.x;
+    s1 += p.y;
+  }
+  const float inv_n = 1.0f / float(R * D);
+  const float a = rnd<T>(s0 * inv_n), b = rnd<T>(s1 * inv_n);
+  if (mse_out) {
+    Elem<T>::store(mse_out + bh, a);       // [2, cfg*H]: spatial
+    Elem<T>::store(mse_out + BH + bh, b);  // temporal
+  }
+  if (best) best[bh] = (b < a) ? 1 : 0;    // argmin, first index on ties
+}
+
+// ---------------------------------------------------------------------------
+// tensor-core path (bf16): scores and probability-times-V on mma.sync
+// m16n8k16 (bf16 x bf16 -> fp32, the reference matmuls' arithmetic) over the
+// 32 sampled rows; 8 warps, a 64-key tile per step.
+// ---------------------------------------------------------------------------
+namespace tcp {
+
+constexpr int kRS = 128 + 8;  // padded row stride (elements) of the bf16 tiles: conflict-free ldmatrix
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// rows [r][D] of a bf16 tensor into a padded shared tile (16-byte pieces)
+template <int D>
+__device__ __forceinline__ void load_rows_bf16(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t bh,
+                                               int64_t T, const int64_t* rows, int nrows) {
+  constexpr int kVec = D / 8;
+  for (int x = threadIdx.x; x < kRows * kVec; x += kThreads) {
+    const int r = x / kVec, c = x % kVec;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < nrows) val = reinterpret_cast<const uint4*>(src + (bh * T + rows[r]) * D)[c];
+    *reinterpret_cast<uint4*>(dst + r * kRS + c * 8) = val;
   }
 }
+template <int D>
+__device__ __forceinline__ void load_tile_bf16(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t bh, int64_t T,
+                                               int64_t j0) {
+  constexpr int kVec = D / 8;
+  for (int x = threadIdx.x; x < kTile * kVec; x += kThreads) {
+    const int j = x / kVec, c = x % kVec;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (j0 + j < T) val = reinterpret_cast<const uint4*>(src + (bh * T + j0 + j) * D)[c];
+    *reinterpret_cast<uint4*>(dst + j * kRS + c * 8) = val;
+  }
+}
+
+// Scores of the warp's 8 keys (keys 8*warp .. +7 of the tile) for all 32
+// rows: s[mt][e] is row 16*mt + gq + 8*(e >= 2), key 8*warp + 2*tq + (e & 1),
+// already rounded as the reference rounds them (-inf past T).
+template <int D>
+__device__ __forceinline__ void tile_scores_tc(const __nv_bfloat16* qs, const __nv_bfloat16* ks, int warp, int lane,
+                                               int64_t j0, const Spec& m, float (&s)[2][4]) {
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[mt][e] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t b[2];
+    {
+      const int mat = (lane >> 3) & 1, i = lane & 7;
+      ldsm_x2(b, ks + (8 * warp + i) * kRS + kk * 16 + mat * 8);
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t a[4];
+      const int mat = lane >> 3, i = lane & 7;
+      ldsm_x4(a, qs + (16 * mt + i + ((mat & 1) ? 8 : 0)) * kRS + kk * 16 + ((mat >= 2) ? 8 : 0));
+      mma16816(s[mt], a, b[0], b[1]);
+    }
+  }
+  const int tq = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t j = j0 + 8 * warp + 2 * tq + (e & 1);
+      s[mt][e] = (j < m.T) ? rnd<__nv_bfloat16>(rnd<__nv_bfloat16>(s[mt][e]) * m.inv_sqrt_d) : -INFINITY;
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) mse_stats_tc_kernel(const __nv_bfloat16* __restrict__ q,
+                                                                const __nv_bfloat16* __restrict__ k,
+                                                                const __grid_constant__ Spec m,
+                                                                float2* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [32][kRS]
+  __nv_bfloat16* ks = qs + kRows * kRS;                                 // [64][kRS]
+  float2* red = reinterpret_cast<float2*>(ks + kTile * kRS);           // [8 warps][3][32]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+  const int64_t bh = blockIdx.y, c = blockIdx.x;
+  load_rows_bf16<D>(qs, q, bh, m.T, m.rows, m.R);
+  Pos qp[4];  // this lane's rows 16*mt + gq + 8*h, x = 2*mt + h
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const int r = 16 * (x >> 1) + gq + 8 * (x & 1);
+    qp[x] = pos_of(m.rows[r < m.R ? r : 0], m);
+  }
+  // per lane: rows 16*mt + gq + 8*h (mt, h in {0, 1}), three variants
+  float mx[4][kVar], sum[4][kVar];
+#pragma unroll
+  for (int x = 0; x < 4; ++x)
+#pragma unroll
+    for (int v = 0; v < kVar; ++v) { mx[x][v] = -INFINITY; sum[x][v] = 0.f; }
+  const int64_t jend = (c + 1) * kChunk < m.T ? (c + 1) * kChunk : m.T;
+  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile) {
+    __syncthreads();
+    load_tile_bf16<D>(ks, k, bh, m.T, j0);
+    __syncthreads();
+    float s[2][4];
+    tile_scores_tc<D>(qs, ks, warp, lane, j0, m, s);
+    const Pos kp[2] = {pos_of(j0 + 8 * warp + 2 * tq, m), pos_of(j0 + 8 * warp + 2 * tq + 1, m)};
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rr = 2 * mt + (e >> 1), r = 16 * mt + gq + 8 * (e >> 1);
+        const int64_t j = j0 + 8 * warp + 2 * tq + (e & 1);
+        if (r >= m.R || j >= m.T) continue;
+        const float xv = s[mt][e];
+#pragma unroll
+        for (int v = 0; v < kVar; ++v) {
+          if (!allowed_pos(v, qp[rr], kp[e & 1], m)) continue;
+          if (xv > mx[rr][v]) {
+            sum[rr][v] = sum[rr][v] * expf(mx[rr][v] - xv) + 1.f;
+            mx[rr][v] = xv;
+          } else {
+            sum[rr][v] += expf(xv - mx[rr][v]);
+          }
+        }
+      }
+  }
+  // combine the 4 lanes of a row (fixed butterfly), then the 8 warps in order
+#pragma unroll
+  for (int x = 0; x < 4; ++x)
+#pragma unroll
+    for (int v = 0; v < kVar; ++v) {
+      float a = mx[x][v], b = sum[x][v];
+#pragma unroll
+      for (int off = 1; off < 4; off <<= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, a, off), ob = __shfl_xor_sync(0xffffffffu, b, off);
+        const float nm = fmaxf(a, oa);
+        b = (nm == -INFINITY) ? 0.f : b * expf(a - nm) + ob * expf(oa - nm);
+        a = nm;
+      }
+      const int r = 16 * (x >> 1) + gq + 8 * (x & 1);
+      if (tq == 0) red[(warp * kVar + v) * kRows + r] = make_float2(a, b);
+    }
+  __syncthreads();
+  if (threadIdx.x < kVar * kRows) {
+    const int t = threadIdx.x;  // v * 32 + r
+    float a = -INFINITY, b = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      const float2 p = red[w * kVar * kRows + t];
+      const float nm = fmaxf(a, p.x);
+      b = (nm == -INFINITY) ? 0.f : b * expf(a - nm) + p.y * expf(p.x - nm);
+      a = nm;
+    }
+    part[(bh * gridDim.x + c) * kVar * kRows + t] = make_float2(a, b);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) mse_pv_tc_kernel(const __nv_bfloat16* __restrict__ q,
+                                                             const __nv_bfloat16* __restrict__ k,
+                                                             const __nv_bfloat16* __restrict__ v,
+                                                             const __grid_constant__ Spec m,
+                                                             const float2* __restrict__ ml,
+                                                             float* __restrict__ acc_out) {
+  constexpr int kPS = kTile + 8;  // padded stride of the probability tiles
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [32][kRS]
+  __nv_bfloat16* ks = qs + kRows * kRS;                                 // [64][kRS]
+  __nv_bfloat16* vs = ks + kTile * kRS;                                 // [64][kRS]
+  __nv_bfloat16* ps = vs + kTile * kRS;                                 // [3][32][kPS]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+  const int64_t bh = blockIdx.y, c = blockIdx.x;
+  load_rows_bf16<D>(qs, q, bh, m.T, m.rows, m.R);
+  float2 mlr[4][kVar];  // (M, L) of this lane's rows
+  Pos qp[4];
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const int r = 16 * (x >> 1) + gq + 8 * (x & 1);
+    qp[x] = pos_of(m.rows[r < m.R ? r : 0], m);
+#pragma unroll
+    for (int vv = 0; vv < kVar; ++vv) mlr[x][vv] = ml[(bh * kVar + vv) * kRows + r];
+  }
+  // output columns of this warp: D / 8 warps, 16 (D=128) or 8 (D=64) per warp
+  constexpr int kNT = D / 64;  // n-tiles of 8 columns per warp
+  float acc[kVar][2][kNT][4];
+#pragma unroll
+  for (int vv = 0; vv < kVar; ++vv)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[vv][mt][nt][e] = 0.f;
+  const int64_t jend = (c + 1) * kChunk < m.T ? (c + 1) * kChunk : m.T;
+  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile) {
+    __syncthreads();
+    load_tile_bf16<D>(ks, k, bh, m.T, j0);
+    load_tile_bf16<D>(vs, v, bh, m.T, j0);
+    __syncthreads();
+    float s[2][4];
+    tile_scores_tc<D>(qs, ks, warp, lane, j0, m, s);
+    const Pos kp[2] = {pos_of(j0 + 8 * warp + 2 * tq, m), pos_of(j0 + 8 * warp + 2 * tq + 1, m)};
+    // p = round(exp(s - M) / L), 0 where the mask (or T) excludes the key
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int x = 2 * mt + h, r = 16 * mt + gq + 8 * h;
+        const int jl = 8 * warp + 2 * tq;
+#pragma unroll
+        for (int vv = 0; vv < kVar; ++vv) {
+          float p2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int64_t j = j0 + jl + u;
+            p2[u] = (r < m.R && j < m.T && allowed_pos(vv, qp[x], kp[u], m))
+                        ? expf(s[mt][2 * h + u] - mlr[x][vv].x) / mlr[x][vv].y : 0.f;
+          }
+          *reinterpret_cast<uint32_t*>(ps + (vv * kRows + r) * kPS + jl) = pack_bf16x2(p2[0], p2[1]);
+        }
+      }
+    __syncthreads();
+    // acc[vv] += P[vv] (32 x 64) . V (64 x D): this warp's columns
+#pragma unroll
+    for (int kk = 0; kk < kTile / 16; ++kk) {
+      uint32_t bf[kNT == 2 ? 4 : 2];
+      {
+        const int mat = lane >> 3, i = lane & 7;
+        const int row = kk * 16 + i + ((mat & 1) ? 8 : 0);
+        const int col = warp * 8 * kNT + ((mat >= 2) ? 8 : 0);
+        if constexpr (kNT == 2) {
+          ldsm_x4_trans(bf, vs + row * kRS + col);
+        } else {
+          uint32_t t4[4];
+          ldsm_x4_trans(t4, vs + row * kRS + col);
+          bf[0] = t4[0];
+          bf[1] = t4[1];
+        }
+      }
+#pragma unroll
+      for (int vv = 0; vv < kVar; ++vv)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t a[4];
+          const int mat = lane >> 3, i = lane & 7;
+          ldsm_x4(a, ps + (vv * kRows + 16 * mt + i + ((mat & 1) ? 8 : 0)) * kPS + kk * 16 + ((mat >= 2) ? 8 : 0));
+          mma16816(acc[vv][mt][0], a, bf[0], bf[1]);
+          if constexpr (kNT == 2) mma16816(acc[vv][mt][1], a, bf[2], bf[3]);
+        }
+    }
+  }
+#pragma unroll
+  for (int vv = 0; vv < kVar; ++vv)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = 16 * mt + gq + 8 * (e >> 1);
+          const int col = warp * 8 * kNT + 8 * nt + 2 * tq + (e & 1);
+          acc_out[(((bh * gridDim.x + c) * kVar + vv) * kRows + r) * D + col] = acc[vv][mt][nt][e];
+        }
+}
+
+template <int D>
+size_t stats_smem() { return size_t(kRows + kTile) * kRS * 2 + size_t(kThreads / 32) * kVar * kRows * 8; }
+template <int D>
+size_t pv_smem() { return size_t(kRows + 2 * kTile) * kRS * 2 + size_t(kVar) * kRows * (kTile + 8) * 2; }
+
+}  // namespace tcp
 
 template <int D>
 size_t stats_smem() { return sizeof(float) * (kRows * D + kTile * (D + 1)); }
@@ -298,12 +631,13 @@ size_t pv_smem() { return sizeof(float) * (kRows * D + kTile * (D + 1) + kTile *
 
 }  // namespace cls
 
-// workspace: chunk statistics | (M, L) | chunk partial outputs
+// workspace: chunk statistics | (M, L) | chunk partial outputs | slice sums
 size_t sample_mse_workspace(int64_t BH, int64_t T, int D) {
   const int64_t nc = cdiv(T, cls::kChunk);
   size_t o = align256(size_t(BH) * nc * cls::kVar * cls::kRows * sizeof(float2));
   o += align256(size_t(BH) * cls::kVar * cls::kRows * sizeof(float2));
   o += align256(size_t(BH) * nc * cls::kVar * cls::kRows * D * sizeof(float));
+  o += align256(size_t(BH) * cdiv(cls::kRows * D, cls::kThreads) * sizeof(float2));
   return o;
 }
 
@@ -318,19 +652,36 @@ static cudaError_t launch_sample_mse_t(cudaStream_t st, const void* q, const voi
   float2* ml = reinterpret_cast<float2*>(w);
   w += align256(size_t(BH) * kVar * kRows * sizeof(float2));
   float* acc = reinterpret_cast<float*>(w);
+  w += align256(size_t(BH) * nc * kVar * kRows * D * sizeof(float));
+  float2* slices = reinterpret_cast<float2*>(w);
+  const int nslices = int(cdiv(kRows * D, kThreads));
   const dim3 grid{unsigned(nc), unsigned(BH), 1u};
-  auto k1 = mse_stats_kernel<T, D>;
-  auto k3 = mse_pv_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(stats_smem<D>()));
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pv_smem<D>()));
-  if (e != cudaSuccess) return e;
   const T* qt = static_cast<const T*>(q);
   const T* kt = static_cast<const T*>(k);
   const T* vt = static_cast<const T*>(v);
-  k1<<<grid, kThreads, stats_smem<D>(), st>>>(qt, kt, m, part);
-  mse_combine_kernel<<<unsigned(BH), 128, 0, st>>>(part, nc, ml);
-  k3<<<grid, kThreads, pv_smem<D>(), st>>>(qt, kt, vt, m, ml, acc);
-  mse_finish_kernel<T, D><<<unsigned(BH), kThreads, 0, st>>>(acc, nc, m.R, BH, static_cast<T*>(mse_out), best);
+  cudaError_t e;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {  // scores and P.V on the tensor cores
+    auto k1 = tcp::mse_stats_tc_kernel<D>;
+    auto k3 = tcp::mse_pv_tc_kernel<D>;
+    e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcp::stats_smem<D>()));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcp::pv_smem<D>()));
+    if (e != cudaSuccess) return e;
+    k1<<<grid, kThreads, tcp::stats_smem<D>(), st>>>(qt, kt, m, part);
+    mse_combine_kernel<<<unsigned(BH), 128, 0, st>>>(part, nc, ml);
+    k3<<<grid, kThreads, tcp::pv_smem<D>(), st>>>(qt, kt, vt, m, ml, acc);
+  } else {
+    auto k1 = mse_stats_kernel<T, D>;
+    auto k3 = mse_pv_kernel<T, D>;
+    e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(stats_smem<D>()));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pv_smem<D>()));
+    if (e != cudaSuccess) return e;
+    k1<<<grid, kThreads, stats_smem<D>(), st>>>(qt, kt, m, part);
+    mse_combine_kernel<<<unsigned(BH), 128, 0, st>>>(part, nc, ml);
+    k3<<<grid, kThreads, pv_smem<D>(), st>>>(qt, kt, vt, m, ml, acc);
+  }
+  mse_finish_part_kernel<T, D><<<dim3(unsigned(nslices), unsigned(BH), 1u), kThreads, 0, st>>>(acc, nc, m.R, slices);
+  mse_finish_kernel<T, D><<<unsigned(BH), 32, 0, st>>>(slices, nslices, m.R, BH, static_cast<T*>(mse_out), best);
   return cudaGetLastError();
 }
 

@@ -269,3 +269,39 @@ def test_piecewise_alias(cuda_device):
     a = ops.piecewise_sparse_attention(q, k, v, density=0.25, block_size=64, use_random=False)
     b = ops.pisa_pg_attention(q, k, v, density=0.25)
     assert torch.equal(a, b)
+
+
+def test_running_max_jumps_in_early_steps(cuda_device):
+    """Keys repeated across the frames of a patch (a temporal head after the
+    token placement) give each query block a few keys with logits ~60 (log2
+    units) above the rest, met a few steps into the walk: the running maximum
+    jumps at steps 2 and 3 of a tile, and the output accumulator is rescaled
+    while the tensor core may still be adding earlier steps into it.  Forty
+    calls (with the allocator churned in between) must all give the same
+    output, within the tolerance of the oracle."""
+    from oracle.layout_oracle import place_reference
+
+    H, ctx, F_, S, D, density = 4, 64, 4, 512, 128, 0.2
+    T = ctx + F_ * S
+    g = torch.Generator().manual_seed(21)
+    q, k, v = (torch.randn(1, H, T, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    for h in (1, 3):
+        base = torch.randn(S, D, generator=g) * 2
+        k[0, h, :F_ * S] = base.repeat(F_, 1).to(torch.bfloat16)
+        q[0, h, :F_ * S] = (base.repeat(F_, 1) + 0.2 * torch.randn(F_ * S, D, generator=g)).to(torch.bfloat16)
+    temporal = torch.tensor([[0, 1, 1, 1]])
+    q, k, v = (place_reference(t.float(), temporal, ctx, F_, S).to(torch.bfloat16) for t in (q, k, v))
+    ref = O.pisa_pg_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), density=density,
+                              dtype="bf16")
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    first = None
+    for it in range(40):
+        junk = torch.full((64 << 20,), it % 251, dtype=torch.uint8, device=cuda_device)
+        del junk
+        o = ops.pisa_pg_attention(qd, kd, vd, density=density)
+        torch.cuda.synchronize()
+        if first is None:
+            first = o.clone()
+            err, cos = _close(_np(o), ref)
+            assert err <= TOL_ABS and cos >= TOL_COS, (err, cos)
+        assert torch.equal(o, first), it
