@@ -93,14 +93,19 @@ struct Cfg {
   static constexpr int kSK = PASA_ATTN_SK;              // K ring slots
   static constexpr int kSV = PASA_ATTN_SV;              // V ring slots
   static constexpr int kKVRegion = (kSK + kSV) * kPairBytes;
-  // Phase 2 has two rings, aliased on the K and V rings: kc rows (read by
-  // the score MMAs) and vc rows + H (read by the P.V issuer).  Each is
-  // released by its own reader, so the next groups' kc need not wait for
-  // the correction MMAs of an earlier group to free a shared slot.
+  // Phase 2 has two rings: vc rows + H (read by the P.V issuer), aliased
+  // on the K and V rings, and kc rows (read by the score MMAs) in memory of
+  // their own.  Each is released by its own reader, so the next groups' kc
+  // need not wait for the correction MMAs of an earlier group to free a
+  // shared slot.  The vc/H ring takes the whole K/V region: a group's 40 KB
+  // land ~3000 cycles after their slot frees, and the P.V issuer waits for
+  // them, so the ring depth sets the phase-2 period (three slots: ~1450
+  // cycles per group; four: the issue rate).  Its own kc ring also lets the
+  // first groups' kc load while phase 1 still runs.
   static constexpr int kSlotH = kCBytes + kHBytes;      // vc rows and H of one group
-  static constexpr int kSH = 3;                         // vc/H ring slots
-  static constexpr int kSCFit = (kKVRegion - kSH * kSlotH) / kCBytes;
-  static constexpr int kSC = kSCFit < 8 ? kSCFit : 8;   // kc ring slots
+  static constexpr int kSHFit = kKVRegion / kSlotH;
+  static constexpr int kSH = kSHFit < 6 ? kSHFit : 6;   // vc/H ring slots
+  static constexpr int kSC = 2;                         // kc ring slots
   static constexpr int kLagH = PASA_ATTN_LAG_H;         // kc loads run this many groups ahead of vc/H
   // TMEM columns
   static constexpr uint32_t kColO = 0;
@@ -112,9 +117,9 @@ struct Cfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;                      // K ring, then V ring
   static constexpr int kOffV = kOffK + kSK * kPairBytes;
-  static constexpr int kOffRingC = kOffK;                            // aliased on the K and V rings
-  static constexpr int kOffRingH = kOffRingC + kSC * kCBytes;
-  static constexpr int kOffUnion = kOffK + kKVRegion;                // u16 [kMaxNT]
+  static constexpr int kOffRingH = kOffK;                            // aliased on the K and V rings
+  static constexpr int kOffRingC = kOffK + kKVRegion;                // kc ring, its own memory
+  static constexpr int kOffUnion = kOffRingC + kSC * kCBytes;        // u16 [kMaxNT]
   static constexpr int kOffMask = kOffUnion + kMaxNT * 2;            // u32 [2][kMaxNG]
   static constexpr int kOffXch = kOffMask + 2 * kMaxNG * 4;          // f32 [2 slots][2 sets][128]
   static constexpr int kOffHand = kOffXch + 2 * 2 * kRowsPerTile * 4;  // f32 [2 sets][m_used, m_true][128]
@@ -122,7 +127,10 @@ struct Cfg {
   static constexpr int kNumBars = 2 * kSK + 2 * kSV + 2 * kSC + 2 * kSH + 1 + 2 + 2 + 2 + 2;
   static constexpr int kOffSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffSlot + 16 + 1024;  // + alignment slack
-  static_assert(kSC >= kSH + kLagH && kOffRingH + kSH * kSlotH <= kOffK + kKVRegion, "phase-2 rings");
+  // (the producer issues kc(i) before vc/H(i - kLagH); kc(i) waits for the
+  // score MMAs of group i - kSC, whose chain of waits reaches back only to
+  // vc/H loads issued before it while kLagH <= kSC + 3)
+  static_assert(kLagH <= kSC + 3 && kSH >= 3 && kOffRingH + kSH * kSlotH <= kOffK + kKVRegion, "phase-2 rings");
   static_assert(kColS0 + 2 * 128 <= kTmemCols, "TMEM budget");
   static_assert(kColO + D <= kColP, "O must fit below P");
   static_assert(kColU + D / 2 <= 128, "U must fit in the S buffer");
@@ -154,7 +162,7 @@ struct Params {
 // Optional step tracer (compile with -DPASA_TRACE): one CTA, chosen with
 // pasa_trace_select(), records SM clock stamps of its pipeline events for
 // the first kTraceSteps steps into g_pasa_trace[event][step]: 0 producer
-// issue (K), 1 S issue, 28 S issued, 2 P.V issue, 29 P.V issued, 3 V issue,
+// issue (K; kc in phase 2), 1 S issue, 28 S issued, 2 P.V issue, 29 P.V issued, 3 V issue (vc/H in phase 2),
 // 4+w softmax warp w (0-7) sees S, 12+w softmax warp w done, 20-27 set-0
 // sub-stages; pasa_trace_read() copies them out.
 #ifdef PASA_TRACE
@@ -369,7 +377,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         if (p < nP) load_k(p);
         if (ok && p >= PASA_ATTN_KV_LAG) load_v(p - PASA_ATTN_KV_LAG);
       }
-      // ring 2 aliases the K and V rings: all of them must be free
+      // the kc ring has memory of its own: its first groups load while the
+      // last phase-1 steps still run
+      int64_t issued_c = 0, issued_h = 0;
+      auto load_c = [&](int64_t i) {
+        const int s = int(i % C::kSC);
+        if (!mbar_wait_bounded(&empty_c[s], uint32_t((i / C::kSC) & 1) ^ 1u, kPollLimit)) { ok = false; return; }
+        PASA_TRACE_MARK(0, nP + i);
+        unsigned char* st = sm + C::kOffRingC + s * C::kCBytes;
+        mbar_arrive_expect_tx(&full_c[s], C::kCBytes);
+        for (int bx = 0; bx < C::kBoxes; ++bx)
+          tma_load_3d(st + bx * (kGroup * 128), &maps.kc, &full_c[s], bx * 64, int32_t(i * kGroup), int32_t(bh));
+        issued_c = i + 1;
+      };
+      for (int64_t i = 0; i < NG2 && i < C::kSC && ok; ++i) load_c(i);
+      // the vc/H ring aliases the K and V rings: all of them must be free
       for (int64_t p = (nP > C::kSK ? nP - C::kSK : 0); p < nP && ok; ++p)
         if (!mbar_wait_bounded(&empty_k[p % C::kSK], uint32_t((p / C::kSK) & 1), kPollLimit)) ok = false;
       for (int64_t p = (nP > C::kSV ? nP - C::kSV : 0); p < nP && ok; ++p)
@@ -377,22 +399,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       // Phase 2: kc rows of every group through ring C, vc rows and H
       // through ring H, the kc loads kLagH groups ahead in issue order (ring
       // C is released by the score MMAs, which run ahead of the P.V issuer)
-      int64_t issued_c = 0, issued_h = 0;
       for (int64_t i = 0; i < NG2 + C::kLagH && ok; ++i) {
-        if (i < NG2) {
-          const int s = int(i % C::kSC);
-          if (!mbar_wait_bounded(&empty_c[s], uint32_t((i / C::kSC) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
-          PASA_TRACE_MARK(0, nP + i);
-          unsigned char* st = sm + C::kOffRingC + s * C::kCBytes;
-          mbar_arrive_expect_tx(&full_c[s], C::kCBytes);
-          for (int bx = 0; bx < C::kBoxes; ++bx)
-            tma_load_3d(st + bx * (kGroup * 128), &maps.kc, &full_c[s], bx * 64, int32_t(i * kGroup), int32_t(bh));
-          issued_c = i + 1;
+        if (i < NG2 && i >= issued_c) {
+          load_c(i);
+          if (!ok) break;
         }
         const int64_t g = i - C::kLagH;
         if (g >= 0) {
           const int s = int(g % C::kSH);
           if (!mbar_wait_bounded(&empty_h[s], uint32_t((g / C::kSH) & 1) ^ 1u, kPollLimit)) { ok = false; break; }
+          PASA_TRACE_MARK(3, nP + g);
           unsigned char* st = sm + C::kOffRingH + s * C::kSlotH;
           mbar_arrive_expect_tx(&full_h[s], C::kSlotH);
           for (int bx = 0; bx < C::kBoxes; ++bx) {
