@@ -275,7 +275,11 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
 namespace sel_tc {
 constexpr int kRowsTC = 16;      // query blocks per CTA, one warp each for the top-k
 constexpr int kThreadsTC = 512;
-constexpr int kKeyChunk = 128;   // key blocks per scoring pass: 16 warps x 8
+// Two configurations: 64 key blocks per scoring pass (8 scoring warps) with
+// two CTAs per SM where the shared memory of two fits (the Wan shapes), so
+// that one CTA's top-k overlaps the other's scoring loads; else 128 key
+// blocks per pass (all 16 warps score) and one CTA per SM.
+constexpr size_t kTwoPerSmSmem = 113 * 1024;  // per-CTA limit for two CTAs per SM
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -292,30 +296,47 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-template <int D>
+// Shared memory: q rows, a chunk of scaled kc rows and their bias (the
+// scoring stage); histograms and compact lists (the top-k stage); the row
+// keys and mask words.  With kShare the two stages share one region, which
+// makes two CTAs per SM fit at the Wan shapes, so that one CTA's top-k
+// overlaps the other's scoring loads.
+template <int D, int kKeyChunk, bool kShare>
 struct Layout {
   static constexpr int kRS = D + 8;  // padded row stride (elements): conflict-free ldmatrix
   __host__ __device__ static size_t bytes(int64_t NT, int64_t NG, int64_t NS, size_t* off) {
-    size_t o = 0;
-    off[0] = o; o += size_t(kRowsTC) * kRS * 2;           // qs  bf16 [16][RS]
-    off[1] = o; o += size_t(kKeyChunk) * kRS * 2;         // ks  bf16 [128][RS]
-    off[2] = o; o += size_t(kKeyChunk) * 4;               // bias f32 [128]
+    size_t a = 0;
+    off[0] = a; a += size_t(kRowsTC) * kRS * 2;           // qs  bf16 [16][RS]
+    off[1] = a; a += size_t(kKeyChunk) * kRS * 2;         // ks  bf16 [chunk][RS]
+    off[2] = a; a += size_t(kKeyChunk) * 4;               // bias f32 [chunk]
+    if (!kShare) {  // one region after the other
+      off[3] = a; a += size_t(kRowsTC) * NT * 4;          // keys u32 [16][NT]
+      off[4] = a; a += size_t(kRowsTC) * 256 * 4;         // hist
+      off[5] = a; a += size_t(kRowsTC) * NG * 4;          // mask words
+      a = (a + 7) & ~size_t(7);
+      off[6] = a; if (NS <= kCompactMax) a += size_t(kRowsTC) * NS * 8;  // compact lists
+      return a;
+    }
+    size_t b = 0;
+    off[4] = b; b += size_t(kRowsTC) * 256 * 4;           // hist (top-k stage)
+    b = (b + 7) & ~size_t(7);
+    off[6] = b; if (NS <= kCompactMax) b += size_t(kRowsTC) * NS * 8;  // compact lists (top-k stage)
+    size_t o = ((a > b ? a : b) + 15) & ~size_t(15);
     off[3] = o; o += size_t(kRowsTC) * NT * 4;            // keys u32 [16][NT]
-    off[4] = o; o += size_t(kRowsTC) * 256 * 4;           // hist
     off[5] = o; o += size_t(kRowsTC) * NG * 4;            // mask words
-    o = (o + 7) & ~size_t(7);
-    off[6] = o; if (NS <= kCompactMax) o += size_t(kRowsTC) * NS * 8;  // compact lists
     return o;
   }
 };
 
-template <int D>
-__global__ void __launch_bounds__(kThreadsTC, 1) select_tc_kernel(
+template <int D, int kKeyChunk, int kMinBlocks>
+__global__ void __launch_bounds__(kThreadsTC, kMinBlocks) select_tc_kernel(
     const __nv_bfloat16* __restrict__ qc, const __nv_bfloat16* __restrict__ kc, const float* __restrict__ h_norm,
     const float* __restrict__ noise, SelectDims dm, float scale, int use_cov_bias,
     int32_t* __restrict__ indices, uint32_t* __restrict__ sel_mask) {
-  using L = Layout<D>;
+  using L = Layout<D, kKeyChunk, (kMinBlocks > 1)>;
   constexpr int RS = L::kRS;
+  constexpr int kScoreWarps = kKeyChunk / 8;  // one m16n8 tile of 8 key blocks per scoring warp
+  static_assert(kScoreWarps >= 1 && kScoreWarps <= kThreadsTC / 32, "scoring warps");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int64_t NT = dm.NT, NG = dm.NG, NTP = dm.NTP, NS = dm.NS;
   size_t off[7];
@@ -387,8 +408,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1) select_tc_kernel(
     }
     if (j0 + kKeyChunk < NT) fetch(j0 + kKeyChunk);
     __syncthreads();
+    if (warp >= kScoreWarps) continue;  // warp-uniform; the loop's barrier is at its top
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const int kb = warp * 8;  // this warp's 8 key blocks within the chunk
+    const int kb = warp * 8;  // this scoring warp's 8 key blocks within the chunk
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t a[4], b[2];
@@ -422,18 +444,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1) select_tc_kernel(
 }
 }  // namespace sel_tc
 
-template <int D>
+template <int D, int kKeyChunk, int kMinBlocks>
 static size_t select_tc_smem(const SelectDims& dm) {
   size_t off[7];
-  return sel_tc::Layout<D>::bytes(dm.NT, dm.NG, dm.NS, off);
+  return sel_tc::Layout<D, kKeyChunk, (kMinBlocks > 1)>::bytes(dm.NT, dm.NG, dm.NS, off);
 }
 
-template <int D>
+template <int D, int kKeyChunk, int kMinBlocks>
 static cudaError_t launch_select_tc_t(cudaStream_t st, const void* qc, const void* kc, const float* hn,
                                       const float* noise, int64_t BH, SelectDims dm, float scale, int use_cov_bias,
                                       int32_t* idx, uint32_t* mask) {
-  const size_t smem = select_tc_smem<D>(dm);
-  auto kern = sel_tc::select_tc_kernel<D>;
+  const size_t smem = select_tc_smem<D, kKeyChunk, kMinBlocks>(dm);
+  auto kern = sel_tc::select_tc_kernel<D, kKeyChunk, kMinBlocks>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   dim3 grid{unsigned(cdiv(dm.NT, sel_tc::kRowsTC)), unsigned(BH), 1u};
@@ -441,6 +463,22 @@ static cudaError_t launch_select_tc_t(cudaStream_t st, const void* qc, const voi
                                                static_cast<const __nv_bfloat16*>(kc), hn, noise, dm, scale,
                                                use_cov_bias, idx, mask);
   return cudaGetLastError();
+}
+
+// The tensor-core selection of one head dimension: two CTAs per SM when
+// they fit, else one, else (rows too long for shared memory) false.
+template <int D>
+static bool launch_select_tc_any(cudaError_t* err, cudaStream_t st, const void* qc, const void* kc, const float* hn,
+                                 const float* noise, int64_t BH, SelectDims dm, float scale, int use_cov_bias,
+                                 int32_t* idx, uint32_t* mask) {
+  constexpr size_t kMaxSmem = 227 * 1024;
+  if (select_tc_smem<D, 64, 2>(dm) <= sel_tc::kTwoPerSmSmem)
+    *err = launch_select_tc_t<D, 64, 2>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+  else if (select_tc_smem<D, 128, 1>(dm) <= kMaxSmem)
+    *err = launch_select_tc_t<D, 128, 1>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+  else
+    return false;
+  return true;
 }
 
 size_t select_smem_bytes(int D, int64_t NT, int64_t NG, int64_t NS) {
@@ -471,11 +509,11 @@ cudaError_t launch_select(cudaStream_t st, int dtype, int D, const void* qc, con
   SelectDims dm;
   dm.NT = NT; dm.NG = cdiv(NT, kGroup); dm.NTP = dm.NG * kGroup; dm.NS = NS; dm.D = D;
   if (dtype == PASA_BF16) {
-    constexpr size_t kMaxSmem = 227 * 1024;
-    if (D == 64 && select_tc_smem<64>(dm) <= kMaxSmem)
-      return launch_select_tc_t<64>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
-    if (D == 128 && select_tc_smem<128>(dm) <= kMaxSmem)
-      return launch_select_tc_t<128>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
+    cudaError_t e = cudaSuccess;
+    if (D == 64 && launch_select_tc_any<64>(&e, st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask))
+      return e;
+    if (D == 128 && launch_select_tc_any<128>(&e, st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask))
+      return e;
     if (D == 64) return launch_select_t<__nv_bfloat16, 64>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
     return launch_select_t<__nv_bfloat16, 128>(st, qc, kc, hn, noise, BH, dm, scale, use_cov_bias, idx, mask);
   }
