@@ -8,7 +8,7 @@
 
 namespace pasa {
 cudaError_t launch_prep(cudaStream_t, int, int, const void*, const void*, const void*, int64_t, int64_t, void*,
-                        void*, void*, float*, void*);
+                        void*, void*, float*, void*, uint32_t*);
 cudaError_t launch_select(cudaStream_t, int, int, const void*, const void*, const float*, const float*, int64_t,
                           int64_t, int64_t, float, int, int32_t*, uint32_t*);
 size_t select_smem_bytes(int D, int64_t NT, int64_t NG, int64_t NS);
@@ -128,8 +128,11 @@ int pasa_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dtype, int b
   return PASA_OK;
 }
 
-int pasa_prep(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
-              int dtype, int block, int group, void* qc, void* kc, void* vc, float* h_norm, void* h_group) {
+namespace {
+// pasa_prep with an error word (nullable, device) for the kernel's bounded waits
+int prep_impl(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
+              int dtype, int block, int group, void* qc, void* kc, void* vc, float* h_norm, void* h_group,
+              uint32_t* err) {
   if (block != kBlock || group != kGroup) return PASA_ERR_UNSUPPORTED;
   if (B < 1 || H < 1) return PASA_ERR_SHAPE;
   int st = check_common(B * H, T, D, dtype);
@@ -140,7 +143,13 @@ int pasa_prep(void* stream, const void* q, const void* k, const void* v, int64_t
     return PASA_ERR_ALIGN;
   if ((st = check_device())) return st;
   return cuda_status(launch_prep(static_cast<cudaStream_t>(stream), dtype, D, q, k, v, B * H, T, qc, kc, vc,
-                                 h_norm, h_group));
+                                 h_norm, h_group, err));
+}
+}  // namespace
+
+int pasa_prep(void* stream, const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t T, int D,
+              int dtype, int block, int group, void* qc, void* kc, void* vc, float* h_norm, void* h_group) {
+  return prep_impl(stream, q, k, v, B, H, T, D, dtype, block, group, qc, kc, vc, h_norm, h_group, nullptr);
 }
 
 int pasa_select(void* stream, const void* qc, const void* kc, const float* h_norm, const float* noise, int64_t BH,
@@ -240,10 +249,10 @@ int forward_impl(void* stream, const void* q, const void* k, const void* v, int6
   uint32_t* mask = reinterpret_cast<uint32_t*>(w + L.off_mask);
   uint32_t* err = reinterpret_cast<uint32_t*>(w + L.off_err);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((st = pasa_prep(stream, q, k, v, B, H, T, D, dtype, kBlock, kGroup, qc, kc, vc, hn, hg))) return st;
+  if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
+  if ((st = prep_impl(stream, q, k, v, B, H, T, D, dtype, kBlock, kGroup, qc, kc, vc, hn, hg, err))) return st;
   if ((st = pasa_select(stream, qc, kc, hn, noise, BH, NT, D, dtype, scale, use_cov_bias, NS, idx, mask)))
     return st;
-  if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
   return attn_dispatch(stream, q, k, v, kc, vc, hg, idx, mask, BH, T, D, dtype, scale, NS, o, err, kernel, o_heads,
                        sc);
 }
@@ -340,13 +349,13 @@ int pasa_forward_range(void* stream, const void* q, const void* k, const void* v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the block statistics and the selection cover the touched heads whole
   // (a head shared with another caller's range is prepared by both)
-  if ((st = pasa_prep(stream, at(q, h0), at(k, h0), at(v, h0), 1, BHt, T, D, dtype, kBlock, kGroup, qc, kc, vc, hn,
-                      hg)))
+  if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
+  if ((st = prep_impl(stream, at(q, h0), at(k, h0), at(v, h0), 1, BHt, T, D, dtype, kBlock, kGroup, qc, kc, vc, hn,
+                      hg, err)))
     return st;
   if ((st = pasa_select(stream, qc, kc, hn, noise ? noise + h0 * NT : nullptr, BHt, NT, D, dtype, scale,
                         use_cov_bias, NS, idx, mask)))
     return st;
-  if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return PASA_ERR_CUDA;
   const size_t stat_bytes = size_t(L.NTP) * D * esize_of(dtype), hg_bytes = size_t(L.NG) * D * D * esize_of(dtype);
   // attention: the first and the last head may be partial, the heads between are whole
   int64_t h = h0;

@@ -209,17 +209,13 @@ static cudaError_t launch_prep_t(cudaStream_t st, const void* q, const void* k, 
 }
 
 cudaError_t launch_prep_tc(cudaStream_t st, int D, const void* q, const void* k, const void* v, int64_t BH,
-                           int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg);
+                           int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg, uint32_t* err);
 
 cudaError_t launch_prep(cudaStream_t st, int dtype, int D, const void* q, const void* k, const void* v,
-                        int64_t BH, int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg) {
+                        int64_t BH, int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg, uint32_t* err) {
   const int64_t NT = cdiv(T_len, kBlock), NG = cdiv(NT, kGroup);
-  // bf16: tensor-core kernel (prep_tc.cu); the CUDA-core kernel below serves fp32 inputs
-  if (dtype == PASA_BF16) return launch_prep_tc(st, D, q, k, v, BH, T_len, qc, kc, vc, hn, hg);
-  if (dtype == PASA_BF16) {
-    if (D == 64) return launch_prep_t<__nv_bfloat16, 64>(st, q, k, v, BH, T_len, NT, NG, qc, kc, vc, hn, hg);
-    return launch_prep_t<__nv_bfloat16, 128>(st, q, k, v, BH, T_len, NT, NG, qc, kc, vc, hn, hg);
-  }
+  // bf16: tensor-core kernels (prep_tc.cu); the CUDA-core kernel below serves fp32 inputs
+  if (dtype == PASA_BF16) return launch_prep_tc(st, D, q, k, v, BH, T_len, qc, kc, vc, hn, hg, err);
   if (D == 64) return launch_prep_t<float, 64>(st, q, k, v, BH, T_len, NT, NG, qc, kc, vc, hn, hg);
   return launch_prep_t<float, 128>(st, q, k, v, BH, T_len, NT, NG, qc, kc, vc, hn, hg);
 }

@@ -8,9 +8,16 @@
 // Tiles stream through a two-stage cp.async pipeline so the next block's
 // 48 KB of q, k, v load while the current block computes.  hc itself never
 // reaches HBM.
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace pasa {
+
+namespace tc {
+// 3-D bf16 tensor map over [batch][rows][D], (64 x box_rows x 1) box, 128-byte swizzle (attn_tc.cu)
+bool make_map(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t batch, int box_rows);
+}  // namespace tc
 
 namespace prep_tc {
 
@@ -252,6 +259,275 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
 
 }  // namespace prep_tc
 
+// ---------------------------------------------------------------------------
+// D = 128: k^T v on tcgen05 (UMMA), tiles staged by TMA.
+//
+// A CTA owns one (head, group of 32 blocks), as above, with the same outputs
+// and rounding points; only the order in which h_norm's squares are summed
+// differs.  Per block: warp 0 loads q, k, v (48 KB) into a 4-deep ring;
+// warp 1 issues k^T v (M = 128 dims of k, N = 128 dims of v, K = 64 tokens;
+// both operands MN-major) into one of two TMEM accumulators; eight compute
+// warps take the tree sums from shared memory and then, per accumulator row
+// and half of the columns, form hc = acc - kc (x) vc, its squared norm and
+// the group sum of bf16(hc), which stays in TMEM (128 more columns) until
+// h_group is written.  The MMA of block j+1 runs during the epilogue of
+// block j, and up to four blocks' loads are in flight.
+// ---------------------------------------------------------------------------
+namespace prep_umma {
+
+constexpr int D = 128;
+constexpr int kThreads = 384;             // warp 0 TMA, warp 1 MMA + TMEM, 2-3 idle, 4-11 compute
+constexpr int kComputeWarps = 8;
+constexpr int kCompute = 32 * kComputeWarps;
+constexpr int kStages = 4;
+constexpr int kBox = kBlock * 128;        // [64 rows][64 columns] bf16, 128-byte swizzled rows
+constexpr int kTileBytes = 2 * kBox;      // q, k or v of one block
+constexpr int kStageBytes = 3 * kTileBytes;
+constexpr int kOffF = kStages * kStageBytes;                 // kc_f, vc_f: f32 [2 blocks][2][D]
+constexpr int kOffRed = kOffF + 2 * 2 * D * 4;               // h_norm partials: f32 [2 blocks][8 warps]
+constexpr int kOffBar = kOffRed + 2 * kComputeWarps * 4;
+constexpr int kNumBars = 2 * kStages + 2 + 2;
+constexpr int kOffSlot = kOffBar + kNumBars * 8;
+constexpr int kSmem = kOffSlot + 16 + 1024;                  // + alignment slack
+constexpr uint32_t kColAcc = 0;           // accumulator b at column 128 b
+constexpr uint32_t kColSum = 256;         // group sum of bf16(hc)
+constexpr uint32_t kTmemCols = 512;
+constexpr int kBarCompute = 1;            // named barrier of the compute warps
+static_assert(kSmem <= 232448, "shared memory budget");
+
+struct Maps {
+  CUtensorMap q, k, v;
+};
+
+__device__ uint32_t g_prep_timeout;       // set when a bounded wait gave up and no error word was passed
+
+__device__ __forceinline__ void report_timeout(uint32_t* err) {
+  atomicOr(err ? err : &g_prep_timeout, PASA_DEVERR_WAIT_TIMEOUT);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) prep_umma_kernel(
+    const __grid_constant__ Maps maps, int64_t T_len, int64_t NT, int64_t NG, __nv_bfloat16* __restrict__ qc,
+    __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, float* __restrict__ h_norm,
+    __nv_bfloat16* __restrict__ h_group, uint32_t* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* kc_f = reinterpret_cast<float*>(sm + kOffF);   // [2][D]: then vc_f at + 2 * D
+  float* vc_f = kc_f + 2 * D;
+  float* red = reinterpret_cast<float*>(sm + kOffRed);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint64_t* empty = full + kStages;       // the stage's k, v read by the MMA and its tree sums taken
+  uint64_t* acc_full = empty + kStages;   // [2] k^T v of a block in accumulator b
+  uint64_t* acc_empty = acc_full + 2;     // [2] the compute warps have read accumulator b
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSlot);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t g = blockIdx.x, bh = blockIdx.y, NTP = NG * kGroup;
+  const int64_t j_first = g * kGroup;
+  const int nvalid = int((NT - j_first) < kGroup ? (NT - j_first) : kGroup);  // blocks of this group < NT
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kComputeWarps); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kComputeWarps); }
+    fence_barrier_init();
+  }
+  if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
+  if (warp == 0 && lane == 0) { prefetch_tmap(&maps.q); prefetch_tmap(&maps.k); prefetch_tmap(&maps.v); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int jj = 0; jj < nvalid && ok; ++jj) {
+        const int s = jj % kStages;
+        if (!mbar_wait_bounded(&empty[s], uint32_t((jj / kStages) & 1) ^ 1u)) { ok = false; break; }
+        unsigned char* st = sm + s * kStageBytes;
+        const int32_t t0 = int32_t((j_first + jj) * kBlock);  // rows >= T_len load as zeros
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        for (int bx = 0; bx < 2; ++bx) {
+          tma_load_3d(st + bx * kBox, &maps.q, &full[s], bx * 64, t0, int32_t(bh));
+          tma_load_3d(st + kTileBytes + bx * kBox, &maps.k, &full[s], bx * 64, t0, int32_t(bh));
+          tma_load_3d(st + 2 * kTileBytes + bx * kBox, &maps.v, &full[s], bx * 64, t0, int32_t(bh));
+        }
+        issued = jj + 1;
+      }
+      if (!ok) report_timeout(err);
+      // drain: the last copies land before the CTA can exit
+      for (int jj = (issued > kStages ? issued - kStages : 0); jj < issued; ++jj)
+        mbar_wait_bounded(&full[jj % kStages], uint32_t((jj / kStages) & 1));
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, 128, true, true);
+      bool ok = true;
+      for (int jj = 0; jj < nvalid && ok; ++jj) {
+        const int s = jj % kStages, b = jj & 1;
+        if (!mbar_wait_bounded(&full[s], uint32_t((jj / kStages) & 1))) { ok = false; break; }
+        if (!mbar_wait_bounded(&acc_empty[b], uint32_t((jj >> 1) & 1) ^ 1u)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + s * kStageBytes);
+        // A[a][r] = k[r][a] and B[r][b] = v[r][b]: both tiles are [tokens][dims]
+        // with the dims contiguous, i.e. MN-major; 64-dim boxes kBox apart,
+        // 8-row groups 1024 bytes apart, and each K16 slice 16 rows further on
+        const uint64_t kd = umma_desc_sw128(st + kTileBytes, kBox, 1024);
+        const uint64_t vd = umma_desc_sw128(st + 2 * kTileBytes, kBox, 1024);
+#pragma unroll
+        for (int kk = 0; kk < kBlock / 16; ++kk)
+          mma_ss(tmem + kColAcc + 128u * uint32_t(b), kd + uint64_t((kk * 2048) >> 4), vd + uint64_t((kk * 2048) >> 4),
+                 idesc, kk > 0 ? 1u : 0u);
+        tc_commit(&empty[s]);
+        tc_commit(&acc_full[b]);
+      }
+      if (!ok) report_timeout(err);
+    }
+  } else if (warp >= 4) {
+    // ================= compute warps =================
+    const int cw = warp - 4;                  // 0..7
+    const int quad = warp & 3;                // TMEM lane quadrant this warp may access
+    const int chalf = cw >> 2;                // columns 64 chalf ... 64 chalf + 63 of the accumulator
+    const int a = quad * 32 + lane;           // accumulator row: dimension a of k
+    const uint32_t lane_base = uint32_t(quad * 32) << 16;
+    const int ct = cw * 32 + lane;            // tree-sum task (192 of them: q, k, v x 64 column pairs)
+    bool ok = true;
+    auto wait_bar = [&](uint64_t* bar, uint32_t parity) {
+      if (ok && !mbar_wait_bounded(bar, parity)) { ok = false; report_timeout(err); }
+    };
+    // h_norm of block b from the per-warp partial sums (double-buffered by b's parity)
+    auto finish_norm = [&](int b) {
+      float tot = 0.f;
+      for (int w = 0; w < kComputeWarps; ++w) tot += red[(b & 1) * kComputeWarps + w];
+      h_norm[bh * NT + j_first + b] = __fsqrt_rn(tot);  // :287
+    };
+    {  // the group sum starts at zero
+      uint32_t z[16];
+#pragma unroll
+      for (int x = 0; x < 16; ++x) z[x] = 0u;
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 16) tmem_st16(tmem + lane_base + kColSum + 64 * chalf + c0, z);
+      tmem_wait_st();
+    }
+    for (int jj = 0; jj < kGroup; ++jj) {
+      const int64_t j = j_first + jj;
+      __nv_bfloat16* qc_row = qc + (bh * NTP + j) * D;
+      __nv_bfloat16* kc_row = kc + (bh * NTP + j) * D;
+      __nv_bfloat16* vc_row = vc + (bh * NTP + j) * D;
+      if (jj >= nvalid) {  // zero padding rows (compute_h_group pads hc with zeros)
+        for (int c = ct; c < 3 * D; c += kCompute) {
+          __nv_bfloat16* row = c < D ? qc_row : (c < 2 * D ? kc_row : vc_row);
+          row[c % D] = __float2bfloat16_rn(0.f);
+        }
+        continue;
+      }
+      const int s = jj % kStages;
+      wait_bar(&full[s], uint32_t((jj / kStages) & 1));
+      const unsigned char* st = sm + s * kStageBytes;
+      const int64_t t0 = j * kBlock;
+      const float len = float((T_len - t0 < kBlock) ? (T_len - t0) : int64_t(kBlock));  // BLOCK_SIZE (:91)
+      float* kcf = kc_f + (jj & 1) * D;
+      float* vcf = vc_f + (jj & 1) * D;
+      if (ct < 3 * (D / 2)) {  // two columns per task; a warp's 32 pairs are one 64-column box
+        const int which = ct / (D / 2), c = 2 * (ct % (D / 2));
+        const unsigned char* box = st + which * kTileBytes + (c >> 6) * kBox;
+        const int cc = c & 63;
+        uint32_t x[kBlock];
+#pragma unroll
+        for (int r = 0; r < kBlock; ++r)
+          x[r] = *reinterpret_cast<const uint32_t*>(box + r * 128 + ((((cc >> 3) ^ (r & 7)) << 4) | ((cc & 7) * 2)));
+        // halving tree in bf16, each partial rounded (as prep.cu)
+#pragma unroll
+        for (int n = kBlock; n > 1; n >>= 1)
+#pragma unroll
+          for (int r = 0; r < n / 2; ++r) x[r] = prep_tc::add_bf16x2(x[r], x[r + n / 2]);
+        const uint32_t sum2 = x[0];
+        const float s0 = __uint_as_float(sum2 << 16), s1 = __uint_as_float(sum2 & 0xFFFF0000u);
+        if (which == 0) {
+          *reinterpret_cast<uint32_t*>(qc_row + c) = pack_bf16x2(__fdiv_rn(s0, len), __fdiv_rn(s1, len));
+        } else if (which == 1) {
+          const float m0 = __fdiv_rn(s0, len), m1 = __fdiv_rn(s1, len);
+          kcf[c] = m0;
+          kcf[c + 1] = m1;
+          *reinterpret_cast<uint32_t*>(kc_row + c) = pack_bf16x2(m0, m1);
+        } else {
+          vcf[c] = s0;
+          vcf[c + 1] = s1;
+          *reinterpret_cast<uint32_t*>(vc_row + c) = sum2;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // this warp's reads of the stage are done
+      // kc_f / vc_f of block jj written; the h_norm partials of block jj-1 too
+      named_bar_sync(kBarCompute, kCompute);
+      if (cw == 0 && lane == 0 && jj > 0) finish_norm(jj - 1);
+
+      // epilogue: row a, 64 columns of hc = k^T v - kc (x) vc
+      const int b = jj & 1;
+      wait_bar(&acc_full[b], uint32_t((jj >> 1) & 1));
+      tc_fence_after();
+      const float nk = -kcf[a];
+      const float2 nk2 = make_float2(nk, nk);
+      float2 nsq2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 16) {
+        const int cb = 64 * chalf + c0;
+        uint32_t acc[16], gs[16];
+        tmem_ld16(tmem + lane_base + kColAcc + 128u * uint32_t(b) + cb, acc);
+        tmem_ld16(tmem + lane_base + kColSum + cb, gs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int x = 0; x < 16; x += 2) {
+          const float2 vb = make_float2(vcf[cb + x], vcf[cb + x + 1]);
+          const float2 hc = __ffma2_rn(nk2, vb, make_float2(__uint_as_float(acc[x]), __uint_as_float(acc[x + 1])));  // :106-107
+          nsq2 = __ffma2_rn(hc, hc, nsq2);                                                                     // :110
+          // hc stored in v dtype (:125): both roundings in one conversion
+          const float2 hr = __bfloat1622float2(__floats2bfloat162_rn(hc.x, hc.y));
+          const float2 sum = __fadd2_rn(make_float2(__uint_as_float(gs[x]), __uint_as_float(gs[x + 1])), hr);
+          gs[x] = __float_as_uint(sum.x);
+          gs[x + 1] = __float_as_uint(sum.y);
+        }
+        tmem_st16(tmem + lane_base + kColSum + cb, gs);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      float nsq = nsq2.x + nsq2.y;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) nsq += __shfl_xor_sync(0xffffffffu, nsq, off);
+      if (lane == 0) red[(jj & 1) * kComputeWarps + cw] = nsq;
+    }
+    named_bar_sync(kBarCompute, kCompute);
+    if (cw == 0 && lane == 0 && nvalid > 0) finish_norm(nvalid - 1);
+
+    // h_group = bf16(group sum / 32), row a, this warp's 64 columns (128 contiguous bytes)
+    __nv_bfloat16* hrow = h_group + ((bh * NG + g) * D + a) * D + 64 * chalf;
+#pragma unroll
+    for (int c0 = 0; c0 < 64; c0 += 16) {
+      uint32_t gs[16];
+      tmem_ld16(tmem + lane_base + kColSum + 64 * chalf + c0, gs);
+      tmem_wait_ld();
+      uint4 out[2];
+      uint32_t* ow = reinterpret_cast<uint32_t*>(out);
+#pragma unroll
+      for (int x = 0; x < 8; ++x)
+        ow[x] = pack_bf16x2(__uint_as_float(gs[2 * x]) * (1.0f / kGroup), __uint_as_float(gs[2 * x + 1]) * (1.0f / kGroup));
+      reinterpret_cast<uint4*>(hrow + c0)[0] = out[0];
+      reinterpret_cast<uint4*>(hrow + c0)[1] = out[1];
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace prep_umma
+
 template <int D>
 static cudaError_t launch_prep_tc_t(cudaStream_t st, const void* q, const void* k, const void* v, int64_t BH,
                                     int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg) {
@@ -268,10 +544,30 @@ static cudaError_t launch_prep_tc_t(cudaStream_t st, const void* q, const void* 
   return cudaGetLastError();
 }
 
+static cudaError_t launch_prep_umma(cudaStream_t st, const void* q, const void* k, const void* v, int64_t BH,
+                                    int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg, uint32_t* err) {
+  using namespace prep_umma;
+  const int64_t NT = cdiv(T_len, kBlock), NG = cdiv(NT, kGroup);
+  Maps maps;
+  if (!tc::make_map(&maps.q, q, D, T_len, BH, kBlock) || !tc::make_map(&maps.k, k, D, T_len, BH, kBlock) ||
+      !tc::make_map(&maps.v, v, D, T_len, BH, kBlock))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(prep_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid{unsigned(NG), unsigned(BH), 1u};
+  prep_umma_kernel<<<grid, kThreads, kSmem, st>>>(maps, T_len, NT, NG, static_cast<__nv_bfloat16*>(qc),
+                                                  static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc),
+                                                  hn, static_cast<__nv_bfloat16*>(hg), err);
+  return cudaGetLastError();
+}
+
+// bf16 block statistics: tcgen05 at D = 128, mma.sync at D = 64.  err
+// (nullable, device) receives PASA_DEVERR_WAIT_TIMEOUT if a bounded wait of
+// the tcgen05 kernel gives up.
 cudaError_t launch_prep_tc(cudaStream_t st, int D, const void* q, const void* k, const void* v, int64_t BH,
-                           int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg) {
-  if (D == 64) return launch_prep_tc_t<64>(st, q, k, v, BH, T_len, qc, kc, vc, hn, hg);
-  return launch_prep_tc_t<128>(st, q, k, v, BH, T_len, qc, kc, vc, hn, hg);
+                           int64_t T_len, void* qc, void* kc, void* vc, float* hn, void* hg, uint32_t* err) {
+  if (D == 128) return launch_prep_umma(st, q, k, v, BH, T_len, qc, kc, vc, hn, hg, err);
+  return launch_prep_tc_t<64>(st, q, k, v, BH, T_len, qc, kc, vc, hn, hg);
 }
 
 }  // namespace pasa
