@@ -92,7 +92,11 @@ PASA_API int pasa_workspace_size(int64_t B, int64_t H, int64_t T, int D, int dty
  *   h_norm  [B*H, NT]           fp32 Frobenius norm of k^T v - kc (x) vc
  *   h_group [B*H, NG, D, D]     per-group mean of the per-block matrices
  * qc, kc, vc, h_group have the input dtype.  The per-block matrices
- * themselves are never written to memory.
+ * themselves are never written to memory.  The bf16 D = 128 kernel waits
+ * on its pipeline barriers with a bound; a wait that gives up (a GPU that
+ * stopped answering) ends the kernel with its outputs incomplete.  The
+ * pasa_forward* entry points report that as PASA_DEVERR_WAIT_TIMEOUT in
+ * their error word, like the attention kernel's own waits.
  */
 PASA_API int pasa_prep(void* stream, const void* q, const void* k, const void* v,
               int64_t B, int64_t H, int64_t T, int D, int dtype, int block, int group,
