@@ -264,35 +264,39 @@ __global__ void __launch_bounds__(kThreads, 1) prep_tc_kernel(
 //
 // A CTA owns one (head, group of 32 blocks), as above, with the same outputs
 // and rounding points; only the order in which h_norm's squares are summed
-// differs.  Per block: warp 0 loads q, k, v (48 KB) into a 4-deep ring;
-// warp 1 issues k^T v (M = 128 dims of k, N = 128 dims of v, K = 64 tokens;
-// both operands MN-major) into one of two TMEM accumulators; eight compute
-// warps take the tree sums from shared memory and then, per accumulator row
-// and half of the columns, form hc = acc - kc (x) vc, its squared norm and
-// the group sum of bf16(hc), which stays in TMEM (128 more columns) until
-// h_group is written.  The MMA of block j+1 runs during the epilogue of
-// block j, and up to four blocks' loads are in flight.
+// differs.  Warp-specialised, per block:
+//   * warp 0 loads q, k, v (48 KB) by TMA into a 4-deep ring;
+//   * warp 1 issues k^T v (M = 128 dims of k, N = 128 dims of v, K = 64
+//     tokens; both operands MN-major) into one of two TMEM accumulators;
+//   * six tree-sum warps take the bf16 column sums (qc, kc, vc) from the
+//     ring and leave kc, vc in fp32 for the epilogue (double-buffered);
+//   * four epilogue warps, one accumulator row per thread, form
+//     hc = acc - kc (x) vc, its squared norm and the group sum of bf16(hc),
+//     which stays in TMEM (128 more columns) until h_group is written.
+// So the tree sums of block j+1, the MMA of block j+1 and the epilogue of
+// block j run at the same time, with up to four blocks' loads in flight.
 // ---------------------------------------------------------------------------
 namespace prep_umma {
 
 constexpr int D = 128;
-constexpr int kThreads = 384;             // warp 0 TMA, warp 1 MMA + TMEM, 2-3 idle, 4-11 compute
-constexpr int kComputeWarps = 8;
-constexpr int kCompute = 32 * kComputeWarps;
+constexpr int kThreads = 384;             // warp 0 TMA, 1 MMA + TMEM, 2-7 tree sums, 8-11 epilogue
+constexpr int kSumWarp0 = 2, kSumWarps = 6;
+constexpr int kEpiWarp0 = 8, kEpiWarps = 4;
 constexpr int kStages = 4;
 constexpr int kBox = kBlock * 128;        // [64 rows][64 columns] bf16, 128-byte swizzled rows
 constexpr int kTileBytes = 2 * kBox;      // q, k or v of one block
 constexpr int kStageBytes = 3 * kTileBytes;
 constexpr int kOffF = kStages * kStageBytes;                 // kc_f, vc_f: f32 [2 blocks][2][D]
-constexpr int kOffRed = kOffF + 2 * 2 * D * 4;               // h_norm partials: f32 [2 blocks][8 warps]
-constexpr int kOffBar = kOffRed + 2 * kComputeWarps * 4;
-constexpr int kNumBars = 2 * kStages + 2 + 2;
+constexpr int kOffRed = kOffF + 2 * 2 * D * 4;               // h_norm partials: f32 [2 blocks][4 warps]
+constexpr int kOffBar = kOffRed + 2 * kEpiWarps * 4;
+constexpr int kNumBars = 2 * kStages + 2 + 2 + 2 + 2;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kSmem = kOffSlot + 16 + 1024;                  // + alignment slack
 constexpr uint32_t kColAcc = 0;           // accumulator b at column 128 b
 constexpr uint32_t kColSum = 256;         // group sum of bf16(hc)
 constexpr uint32_t kTmemCols = 512;
-constexpr int kBarCompute = 1;            // named barrier of the compute warps
+constexpr int kBarEpi = 1;                // named barrier of the epilogue warps
+static_assert(kSumWarps * 32 == 3 * (D / 2), "one column pair of q, k or v per tree-sum thread");
 static_assert(kSmem <= 232448, "shared memory budget");
 
 struct Maps {
@@ -315,9 +319,11 @@ __global__ void __launch_bounds__(kThreads, 1) prep_umma_kernel(
   float* vc_f = kc_f + 2 * D;
   float* red = reinterpret_cast<float*>(sm + kOffRed);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
-  uint64_t* empty = full + kStages;       // the stage's k, v read by the MMA and its tree sums taken
-  uint64_t* acc_full = empty + kStages;   // [2] k^T v of a block in accumulator b
-  uint64_t* acc_empty = acc_full + 2;     // [2] the compute warps have read accumulator b
+  uint64_t* empty = full + kStages;         // the stage's k, v read by the MMA and its tree sums taken
+  uint64_t* acc_full = empty + kStages;     // [2] k^T v of a block in accumulator b
+  uint64_t* acc_empty = acc_full + 2;       // [2] the epilogue warps have read accumulator b
+  uint64_t* stats_full = acc_empty + 2;     // [2] kc_f, vc_f of a block in buffer b
+  uint64_t* stats_empty = stats_full + 2;   // [2] the epilogue warps are done with buffer b
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffSlot);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -326,8 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1) prep_umma_kernel(
   const int nvalid = int((NT - j_first) < kGroup ? (NT - j_first) : kGroup);  // blocks of this group < NT
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kComputeWarps); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kComputeWarps); }
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kSumWarps); }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps);
+      mbar_init(&stats_full[b], kSumWarps); mbar_init(&stats_empty[b], kEpiWarps);
+    }
     fence_barrier_init();
   }
   if (warp == 1) { tmem_alloc(tmem_slot, kTmemCols); tmem_relinquish(); }
@@ -385,102 +394,91 @@ __global__ void __launch_bounds__(kThreads, 1) prep_umma_kernel(
       }
       if (!ok) report_timeout(err);
     }
-  } else if (warp >= 4) {
-    // ================= compute warps =================
-    const int cw = warp - 4;                  // 0..7
-    const int quad = warp & 3;                // TMEM lane quadrant this warp may access
-    const int chalf = cw >> 2;                // columns 64 chalf ... 64 chalf + 63 of the accumulator
-    const int a = quad * 32 + lane;           // accumulator row: dimension a of k
-    const uint32_t lane_base = uint32_t(quad * 32) << 16;
-    const int ct = cw * 32 + lane;            // tree-sum task (192 of them: q, k, v x 64 column pairs)
+  } else if (warp < kEpiWarp0) {
+    // ================= tree sums =================
+    const int ct = (warp - kSumWarp0) * 32 + lane;  // q, k, v x 64 column pairs; a warp's pairs are one box
+    const int which = ct / (D / 2), c = 2 * (ct % (D / 2));
+    bool ok = true;
+    for (int jj = 0; jj < kGroup; ++jj) {
+      const int64_t j = j_first + jj;
+      __nv_bfloat16* row = (which == 0 ? qc : which == 1 ? kc : vc) + (bh * NTP + j) * D;
+      if (jj >= nvalid) {  // zero padding rows (compute_h_group pads hc with zeros)
+        *reinterpret_cast<uint32_t*>(row + c) = 0u;
+        continue;
+      }
+      const int s = jj % kStages, b = jj & 1;
+      if (ok && !mbar_wait_bounded(&full[s], uint32_t((jj / kStages) & 1))) { ok = false; report_timeout(err); }
+      // kc_f / vc_f buffer b was last read by the epilogue of block jj - 2
+      if (ok && !mbar_wait_bounded(&stats_empty[b], uint32_t((jj >> 1) & 1) ^ 1u)) { ok = false; report_timeout(err); }
+      const unsigned char* box = sm + s * kStageBytes + which * kTileBytes + (c >> 6) * kBox;
+      const int cc = c & 63;
+      uint32_t x[kBlock];
+#pragma unroll
+      for (int r = 0; r < kBlock; ++r)
+        x[r] = *reinterpret_cast<const uint32_t*>(box + r * 128 + ((((cc >> 3) ^ (r & 7)) << 4) | ((cc & 7) * 2)));
+      // halving tree in bf16, each partial rounded (as prep.cu)
+#pragma unroll
+      for (int n = kBlock; n > 1; n >>= 1)
+#pragma unroll
+        for (int r = 0; r < n / 2; ++r) x[r] = prep_tc::add_bf16x2(x[r], x[r + n / 2]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // this warp's reads of the stage are done
+      const uint32_t sum2 = x[0];
+      const float s0 = __uint_as_float(sum2 << 16), s1 = __uint_as_float(sum2 & 0xFFFF0000u);
+      const int64_t t0 = j * kBlock;
+      const float len = float((T_len - t0 < kBlock) ? (T_len - t0) : int64_t(kBlock));  // BLOCK_SIZE (:91)
+      if (which == 0) {
+        *reinterpret_cast<uint32_t*>(row + c) = pack_bf16x2(__fdiv_rn(s0, len), __fdiv_rn(s1, len));
+      } else if (which == 1) {
+        const float m0 = __fdiv_rn(s0, len), m1 = __fdiv_rn(s1, len);
+        kc_f[b * D + c] = m0;
+        kc_f[b * D + c + 1] = m1;
+        *reinterpret_cast<uint32_t*>(row + c) = pack_bf16x2(m0, m1);
+      } else {
+        vc_f[b * D + c] = s0;
+        vc_f[b * D + c + 1] = s1;
+        *reinterpret_cast<uint32_t*>(row + c) = sum2;
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stats_full[b]);  // release: kc_f / vc_f above precede it
+    }
+  } else {
+    // ================= epilogue =================
+    const int ew = warp - kEpiWarp0;          // 0..3 == warp & 3, the TMEM lane quadrant
+    const int a = ew * 32 + lane;             // accumulator row: dimension a of k
+    const uint32_t lane_base = uint32_t(ew * 32) << 16;
     bool ok = true;
     auto wait_bar = [&](uint64_t* bar, uint32_t parity) {
       if (ok && !mbar_wait_bounded(bar, parity)) { ok = false; report_timeout(err); }
-    };
-    // h_norm of block b from the per-warp partial sums (double-buffered by b's parity)
-    auto finish_norm = [&](int b) {
-      float tot = 0.f;
-      for (int w = 0; w < kComputeWarps; ++w) tot += red[(b & 1) * kComputeWarps + w];
-      h_norm[bh * NT + j_first + b] = __fsqrt_rn(tot);  // :287
     };
     {  // the group sum starts at zero
       uint32_t z[16];
 #pragma unroll
       for (int x = 0; x < 16; ++x) z[x] = 0u;
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) tmem_st16(tmem + lane_base + kColSum + 64 * chalf + c0, z);
+      for (int c0 = 0; c0 < D; c0 += 16) tmem_st16(tmem + lane_base + kColSum + c0, z);
       tmem_wait_st();
     }
-    for (int jj = 0; jj < kGroup; ++jj) {
-      const int64_t j = j_first + jj;
-      __nv_bfloat16* qc_row = qc + (bh * NTP + j) * D;
-      __nv_bfloat16* kc_row = kc + (bh * NTP + j) * D;
-      __nv_bfloat16* vc_row = vc + (bh * NTP + j) * D;
-      if (jj >= nvalid) {  // zero padding rows (compute_h_group pads hc with zeros)
-        for (int c = ct; c < 3 * D; c += kCompute) {
-          __nv_bfloat16* row = c < D ? qc_row : (c < 2 * D ? kc_row : vc_row);
-          row[c % D] = __float2bfloat16_rn(0.f);
-        }
-        continue;
-      }
-      const int s = jj % kStages;
-      wait_bar(&full[s], uint32_t((jj / kStages) & 1));
-      const unsigned char* st = sm + s * kStageBytes;
-      const int64_t t0 = j * kBlock;
-      const float len = float((T_len - t0 < kBlock) ? (T_len - t0) : int64_t(kBlock));  // BLOCK_SIZE (:91)
-      float* kcf = kc_f + (jj & 1) * D;
-      float* vcf = vc_f + (jj & 1) * D;
-      if (ct < 3 * (D / 2)) {  // two columns per task; a warp's 32 pairs are one 64-column box
-        const int which = ct / (D / 2), c = 2 * (ct % (D / 2));
-        const unsigned char* box = st + which * kTileBytes + (c >> 6) * kBox;
-        const int cc = c & 63;
-        uint32_t x[kBlock];
-#pragma unroll
-        for (int r = 0; r < kBlock; ++r)
-          x[r] = *reinterpret_cast<const uint32_t*>(box + r * 128 + ((((cc >> 3) ^ (r & 7)) << 4) | ((cc & 7) * 2)));
-        // halving tree in bf16, each partial rounded (as prep.cu)
-#pragma unroll
-        for (int n = kBlock; n > 1; n >>= 1)
-#pragma unroll
-          for (int r = 0; r < n / 2; ++r) x[r] = prep_tc::add_bf16x2(x[r], x[r + n / 2]);
-        const uint32_t sum2 = x[0];
-        const float s0 = __uint_as_float(sum2 << 16), s1 = __uint_as_float(sum2 & 0xFFFF0000u);
-        if (which == 0) {
-          *reinterpret_cast<uint32_t*>(qc_row + c) = pack_bf16x2(__fdiv_rn(s0, len), __fdiv_rn(s1, len));
-        } else if (which == 1) {
-          const float m0 = __fdiv_rn(s0, len), m1 = __fdiv_rn(s1, len);
-          kcf[c] = m0;
-          kcf[c + 1] = m1;
-          *reinterpret_cast<uint32_t*>(kc_row + c) = pack_bf16x2(m0, m1);
-        } else {
-          vcf[c] = s0;
-          vcf[c + 1] = s1;
-          *reinterpret_cast<uint32_t*>(vc_row + c) = sum2;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);  // this warp's reads of the stage are done
-      // kc_f / vc_f of block jj written; the h_norm partials of block jj-1 too
-      named_bar_sync(kBarCompute, kCompute);
-      if (cw == 0 && lane == 0 && jj > 0) finish_norm(jj - 1);
-
-      // epilogue: row a, 64 columns of hc = k^T v - kc (x) vc
+    for (int jj = 0; jj < nvalid; ++jj) {
       const int b = jj & 1;
+      wait_bar(&stats_full[b], uint32_t((jj >> 1) & 1));
       wait_bar(&acc_full[b], uint32_t((jj >> 1) & 1));
       tc_fence_after();
+      const float* kcf = kc_f + b * D;
+      const float* vcf = vc_f + b * D;
       const float nk = -kcf[a];
       const float2 nk2 = make_float2(nk, nk);
       float2 nsq2 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) {
-        const int cb = 64 * chalf + c0;
+#pragma unroll 2
+      for (int c0 = 0; c0 < D; c0 += 16) {
         uint32_t acc[16], gs[16];
-        tmem_ld16(tmem + lane_base + kColAcc + 128u * uint32_t(b) + cb, acc);
-        tmem_ld16(tmem + lane_base + kColSum + cb, gs);
+        tmem_ld16(tmem + lane_base + kColAcc + 128u * uint32_t(b) + c0, acc);
+        tmem_ld16(tmem + lane_base + kColSum + c0, gs);
         tmem_wait_ld();
 #pragma unroll
         for (int x = 0; x < 16; x += 2) {
-          const float2 vb = make_float2(vcf[cb + x], vcf[cb + x + 1]);
+          const float2 vb = make_float2(vcf[c0 + x], vcf[c0 + x + 1]);
           const float2 hc = __ffma2_rn(nk2, vb, make_float2(__uint_as_float(acc[x]), __uint_as_float(acc[x + 1])));  // :106-107
           nsq2 = __ffma2_rn(hc, hc, nsq2);                                                                     // :110
           // hc stored in v dtype (:125): both roundings in one conversion
@@ -489,26 +487,30 @@ __global__ void __launch_bounds__(kThreads, 1) prep_umma_kernel(
           gs[x] = __float_as_uint(sum.x);
           gs[x + 1] = __float_as_uint(sum.y);
         }
-        tmem_st16(tmem + lane_base + kColSum + cb, gs);
+        tmem_st16(tmem + lane_base + kColSum + c0, gs);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) { mbar_arrive(&acc_empty[b]); mbar_arrive(&stats_empty[b]); }
       float nsq = nsq2.x + nsq2.y;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) nsq += __shfl_xor_sync(0xffffffffu, nsq, off);
-      if (lane == 0) red[(jj & 1) * kComputeWarps + cw] = nsq;
+      if (lane == 0) red[b * kEpiWarps + ew] = nsq;
+      // h_norm of block jj from the four warps' partials, in warp order
+      named_bar_sync(kBarEpi, 32 * kEpiWarps);
+      if (ew == 0 && lane == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < kEpiWarps; ++w) tot += red[b * kEpiWarps + w];
+        h_norm[bh * NT + j_first + jj] = __fsqrt_rn(tot);  // :287
+      }
     }
-    named_bar_sync(kBarCompute, kCompute);
-    if (cw == 0 && lane == 0 && nvalid > 0) finish_norm(nvalid - 1);
-
-    // h_group = bf16(group sum / 32), row a, this warp's 64 columns (128 contiguous bytes)
-    __nv_bfloat16* hrow = h_group + ((bh * NG + g) * D + a) * D + 64 * chalf;
-#pragma unroll
-    for (int c0 = 0; c0 < 64; c0 += 16) {
+    // h_group = bf16(group sum / 32), row a (256 contiguous bytes)
+    __nv_bfloat16* hrow = h_group + ((bh * NG + g) * D + a) * D;
+#pragma unroll 2
+    for (int c0 = 0; c0 < D; c0 += 16) {
       uint32_t gs[16];
-      tmem_ld16(tmem + lane_base + kColSum + 64 * chalf + c0, gs);
+      tmem_ld16(tmem + lane_base + kColSum + c0, gs);
       tmem_wait_ld();
       uint4 out[2];
       uint32_t* ow = reinterpret_cast<uint32_t*>(out);
