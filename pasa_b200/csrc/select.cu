@@ -31,6 +31,54 @@ struct SelectDims {
   int D;
 };
 
+// Winners placed by rank: a warp bitonic sort (descending) of the NS <= 32 P
+// composites (key, then lower index), P per lane at positions P * lane + u;
+// padding 0 sorts last (every composite is > 0: its low word is
+// 0xFFFFFFFF - j with j < 2^24).  Writes the NS indices, best first.
+template <int P>
+__device__ __forceinline__ void bitonic_place(const uint64_t* cl, int64_t NS, int32_t* out) {
+  constexpr int kN = 32 * P;
+  const int lane = threadIdx.x & 31;
+  uint64_t v[P];
+#pragma unroll
+  for (int u = 0; u < P; ++u) {
+    const int64_t i = P * lane + u;
+    v[u] = (i < NS) ? cl[i] : 0ull;
+  }
+#pragma unroll
+  for (int k = 2; k <= kN; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= P) {  // partner in lane ^ (j / P), same slot
+        const int lm = j / P;
+        const bool lower = (lane & lm) == 0;
+#pragma unroll
+        for (int u = 0; u < P; ++u) {
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, v[u], lm);
+          const bool desc = ((P * lane + u) & k) == 0;
+          v[u] = (lower == desc) ? (v[u] > o ? v[u] : o) : (v[u] < o ? v[u] : o);
+        }
+      } else {       // partner in this lane: slot u ^ j
+#pragma unroll
+        for (int u = 0; u < P; ++u) {
+          if ((u & j) != 0) continue;
+          const int w = u | j;
+          const bool desc = ((P * lane + u) & k) == 0;
+          const uint64_t a = v[u], b = v[w];
+          const bool swap = desc ? (a < b) : (a > b);
+          v[u] = swap ? b : a;
+          v[w] = swap ? a : b;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < P; ++u) {
+    const int64_t i = P * lane + u;
+    if (i < NS) out[i] = int32_t(0xFFFFFFFFu - uint32_t(v[u] & 0xFFFFFFFFu));
+  }
+}
+
 // Top-NS of one row of order keys, by one warp: 4-pass radix select of the
 // NS-th largest key, ties at that key taken by ascending block index, then
 // every winner placed at its rank (key descending, index ascending).  Writes
@@ -128,47 +176,9 @@ __device__ __forceinline__ void row_topk(const uint32_t* rk, int64_t NT, int64_t
     }
     __syncwarp();
     if (NS <= 128) {
-      // bitonic sort (descending) of the composites, 4 per lane at positions
-      // 4 * lane + u; padding 0 sorts last (every composite is > 0: its low
-      // word is 0xFFFFFFFF - j with j < 2^24)
-      uint64_t v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t i = 4 * lane + u;
-        v[u] = (i < NS) ? cl[i] : 0ull;
-      }
-#pragma unroll
-      for (int k = 2; k <= 128; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-          if (j >= 4) {  // partner in lane ^ (j / 4), same slot
-            const int lm = j >> 2;
-            const bool lower = (lane & lm) == 0;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const uint64_t o = __shfl_xor_sync(0xffffffffu, v[u], lm);
-              const bool desc = ((4 * lane + u) & k) == 0;
-              v[u] = (lower == desc) ? (v[u] > o ? v[u] : o) : (v[u] < o ? v[u] : o);
-            }
-          } else {       // partner in this lane: slot u ^ j
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              if ((u & j) != 0) continue;
-              const int w = u | j;
-              const bool desc = ((4 * lane + u) & k) == 0;
-              const uint64_t a = v[u], b = v[w];
-              const bool swap = desc ? (a < b) : (a > b);
-              v[u] = swap ? b : a;
-              v[w] = swap ? a : b;
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t i = 4 * lane + u;
-        if (i < NS) out[i] = int32_t(0xFFFFFFFFu - uint32_t(v[u] & 0xFFFFFFFFu));
-      }
+      bitonic_place<4>(cl, NS, out);
+    } else if (NS <= 256) {
+      bitonic_place<8>(cl, NS, out);
     } else {
       for (int64_t e = lane; e < NS; e += 32) {
         const uint64_t me = cl[e];
