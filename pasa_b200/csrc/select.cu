@@ -128,25 +128,61 @@ __device__ __forceinline__ void row_topk(const uint32_t* rk, int64_t NT, int64_t
     const uint32_t excl = incl - tot;
     const uint32_t hit = __ballot_sync(0xffffffffu, incl >= remaining);
     const int src = __ffs(hit) - 1;  // first lane whose range reaches `remaining`
-    uint32_t bucket = 0, above = 0;
+    uint32_t bucket = 0, above = 0, bcount = 0;
     if (lane == src) {
       uint32_t c = excl;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        if (c + cnt[u] >= remaining) { bucket = 255 - 8 * lane - u; above = c; break; }
+        if (c + cnt[u] >= remaining) { bucket = 255 - 8 * lane - u; above = c; bcount = cnt[u]; break; }
         c += cnt[u];
       }
     }
     bucket = __shfl_sync(0xffffffffu, bucket, src);
     above = __shfl_sync(0xffffffffu, above, src);
+    bcount = __shfl_sync(0xffffffffu, bcount, src);
     remaining -= above;
     prefix |= bucket << shift;
     pmask |= 0xFFu << shift;
     __syncwarp();
+    if (hi >= 0 && bcount <= 32u) {
+      // The boundary bucket holds at most 32 keys: gather them, one per lane
+      // (the histogram is free now), and sort them descending across the
+      // warp; the remaining-th of them is the NS-th largest key of the row.
+      uint32_t got = 0;
+      for (int64_t j0 = 0; j0 < NT; j0 += 32) {
+        const int64_t j = j0 + lane;
+        const uint32_t kj = (j < NT) ? rk[j] : 0u;
+        const bool in = (j < NT) && ((kj & pmask) == prefix);
+        const uint32_t b = __ballot_sync(0xffffffffu, in);
+        if (in) h[got + __popc(b & ((1u << lane) - 1u))] = kj;
+        got += __popc(b);
+      }
+      __syncwarp();
+      // absent lanes hold 0, below every key (an order key of 0 would be a NaN score)
+      uint32_t c = (uint32_t(lane) < bcount) ? h[lane] : 0u;
+#pragma unroll
+      for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+        for (int jx = k >> 1; jx > 0; jx >>= 1) {
+          const uint32_t o = __shfl_xor_sync(0xffffffffu, c, jx);
+          const bool lower = (lane & jx) == 0, desc = (lane & k) == 0;
+          c = (lower == desc) ? (c > o ? c : o) : (c < o ? c : o);
+        }
+      const uint32_t kv = __shfl_sync(0xffffffffu, c, int(remaining) - 1);
+      // candidates above the NS-th key are taken whole; ties at it by index
+      remaining -= uint32_t(__popc(__ballot_sync(0xffffffffu, c > kv)));
+      prefix = kv;
+      pmask = 0xFFFFFFFFu;
+      hi = -1;
+      __syncwarp();
+    }
   }
   const uint32_t kth = prefix;  // key of the NS-th largest score
-  // ties at kth: take the `remaining` lowest block indices
-  uint32_t taken = 0;
+  // ties at kth: take the `remaining` lowest block indices; the same pass
+  // writes the mask words and (NS <= kCompactMax) the compact list of
+  // (key, index) composites of the selected blocks
+  const bool compact = NS <= kCompactMax;
+  uint32_t taken = 0, base = 0;
   for (int64_t j0 = 0; j0 < NT; j0 += 32) {
     const int64_t j = j0 + lane;
     const uint32_t kj = (j < NT) ? rk[j] : 0u;
@@ -157,24 +193,14 @@ __device__ __forceinline__ void row_topk(const uint32_t* rk, int64_t NT, int64_t
     const uint32_t selb = __ballot_sync(0xffffffffu, sel);
     taken += __popc(eqb);
     if (lane == 0) mw[j0 >> 5] = selb;  // j0 is a multiple of 32: one word per step
+    if (compact && sel)  // larger composite = better: key, then lower index
+      cl[base + __popc(selb & ((1u << lane) - 1u))] = (uint64_t(kj) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
+    base += __popc(selb);
   }
   __syncwarp();
 
-  if (NS <= kCompactMax) {
-    // compact (key, index) of the selected blocks, then place by rank
-    uint32_t base = 0;
-    for (int64_t j0 = 0; j0 < NT; j0 += 32) {
-      const int64_t j = j0 + lane;
-      const bool sel = (mw[j0 >> 5] >> lane) & 1u;
-      const uint32_t b = __ballot_sync(0xffffffffu, sel);
-      if (sel) {
-        const uint32_t pos = base + __popc(b & ((1u << lane) - 1u));
-        // larger composite = better: key, then lower index
-        cl[pos] = (uint64_t(rk[j]) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(j));
-      }
-      base += __popc(b);
-    }
-    __syncwarp();
+  if (compact) {
+    // place the compacted winners by rank
     if (NS <= 128) {
       bitonic_place<4>(cl, NS, out);
     } else if (NS <= 256) {
