@@ -380,15 +380,23 @@ __device__ __forceinline__ void load_rows_bf16(__nv_bfloat16* dst, const __nv_bf
     *reinterpret_cast<uint4*>(dst + r * kRS + c * 8) = val;
   }
 }
+// A tile of keys (or values) staged by cp.async (16-byte pieces; rows >= T
+// are zero-filled), so that the next tile's loads run while the current one
+// is used.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+               :: "r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 template <int D>
-__device__ __forceinline__ void load_tile_bf16(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t bh, int64_t T,
-                                               int64_t j0) {
+__device__ __forceinline__ void async_tile_bf16(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t bh, int64_t T,
+                                                int64_t j0) {
   constexpr int kVec = D / 8;
   for (int x = threadIdx.x; x < kTile * kVec; x += kThreads) {
     const int j = x / kVec, c = x % kVec;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (j0 + j < T) val = reinterpret_cast<const uint4*>(src + (bh * T + j0 + j) * D)[c];
-    *reinterpret_cast<uint4*>(dst + j * kRS + c * 8) = val;
+    const bool valid = j0 + j < T;
+    cp_async16(dst + j * kRS + c * 8, src + (valid ? (bh * T + j0 + j) * D + c * 8 : 0), valid);
   }
 }
 
@@ -434,8 +442,8 @@ __global__ void __launch_bounds__(kThreads) mse_stats_tc_kernel(const __nv_bfloa
                                                                 float2* __restrict__ part) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [32][kRS]
-  __nv_bfloat16* ks = qs + kRows * kRS;                                 // [64][kRS]
-  float2* red = reinterpret_cast<float2*>(ks + kTile * kRS);           // [8 warps][3][32]
+  __nv_bfloat16* ks2 = qs + kRows * kRS;                                // [2 buffers][64][kRS]
+  float2* red = reinterpret_cast<float2*>(ks2 + 2 * kTile * kRS);      // [8 warps][3][32]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
   const int64_t bh = blockIdx.y, c = blockIdx.x;
   load_rows_bf16<D>(qs, q, bh, m.T, m.rows, m.R);
@@ -452,10 +460,16 @@ __global__ void __launch_bounds__(kThreads) mse_stats_tc_kernel(const __nv_bfloa
 #pragma unroll
     for (int v = 0; v < kVar; ++v) { mx[x][v] = -INFINITY; sum[x][v] = 0.f; }
   const int64_t jend = (c + 1) * kChunk < m.T ? (c + 1) * kChunk : m.T;
-  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile) {
+  int buf = 0;
+  async_tile_bf16<D>(ks2, k, bh, m.T, c * kChunk);
+  cp_async_commit();
+  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile, buf ^= 1) {
+    __syncthreads();  // the tile before was read by every warp: its buffer may be refilled
+    if (j0 + kTile < jend) async_tile_bf16<D>(ks2 + (buf ^ 1) * kTile * kRS, k, bh, m.T, j0 + kTile);
+    cp_async_commit();
+    cp_async_wait1();  // this thread's copies of tile j0 have landed
     __syncthreads();
-    load_tile_bf16<D>(ks, k, bh, m.T, j0);
-    __syncthreads();
+    const __nv_bfloat16* ks = ks2 + buf * kTile * kRS;
     float s[2][4];
     tile_scores_tc<D>(qs, ks, warp, lane, j0, m, s);
     const Pos kp[2] = {pos_of(j0 + 8 * warp + 2 * tq, m), pos_of(j0 + 8 * warp + 2 * tq + 1, m)};
@@ -519,9 +533,9 @@ __global__ void __launch_bounds__(kThreads) mse_pv_tc_kernel(const __nv_bfloat16
   constexpr int kPS = kTile + 8;  // padded stride of the probability tiles
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [32][kRS]
-  __nv_bfloat16* ks = qs + kRows * kRS;                                 // [64][kRS]
-  __nv_bfloat16* vs = ks + kTile * kRS;                                 // [64][kRS]
-  __nv_bfloat16* ps = vs + kTile * kRS;                                 // [3][32][kPS]
+  __nv_bfloat16* ks2 = qs + kRows * kRS;                                // [2 buffers][64][kRS]
+  __nv_bfloat16* vs2 = ks2 + 2 * kTile * kRS;                           // [2 buffers][64][kRS]
+  __nv_bfloat16* ps = vs2 + 2 * kTile * kRS;                            // [3][32][kPS]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
   const int64_t bh = blockIdx.y, c = blockIdx.x;
   load_rows_bf16<D>(qs, q, bh, m.T, m.rows, m.R);
@@ -546,11 +560,21 @@ __global__ void __launch_bounds__(kThreads) mse_pv_tc_kernel(const __nv_bfloat16
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[vv][mt][nt][e] = 0.f;
   const int64_t jend = (c + 1) * kChunk < m.T ? (c + 1) * kChunk : m.T;
-  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile) {
+  int buf = 0;
+  async_tile_bf16<D>(ks2, k, bh, m.T, c * kChunk);
+  async_tile_bf16<D>(vs2, v, bh, m.T, c * kChunk);
+  cp_async_commit();
+  for (int64_t j0 = c * kChunk; j0 < jend; j0 += kTile, buf ^= 1) {
+    __syncthreads();  // the tile before (and its probabilities) were read by every warp
+    if (j0 + kTile < jend) {
+      async_tile_bf16<D>(ks2 + (buf ^ 1) * kTile * kRS, k, bh, m.T, j0 + kTile);
+      async_tile_bf16<D>(vs2 + (buf ^ 1) * kTile * kRS, v, bh, m.T, j0 + kTile);
+    }
+    cp_async_commit();
+    cp_async_wait1();  // this thread's copies of tile j0 have landed
     __syncthreads();
-    load_tile_bf16<D>(ks, k, bh, m.T, j0);
-    load_tile_bf16<D>(vs, v, bh, m.T, j0);
-    __syncthreads();
+    const __nv_bfloat16* ks = ks2 + buf * kTile * kRS;
+    const __nv_bfloat16* vs = vs2 + buf * kTile * kRS;
     float s[2][4];
     tile_scores_tc<D>(qs, ks, warp, lane, j0, m, s);
     const Pos kp[2] = {pos_of(j0 + 8 * warp + 2 * tq, m), pos_of(j0 + 8 * warp + 2 * tq + 1, m)};
@@ -618,9 +642,9 @@ __global__ void __launch_bounds__(kThreads) mse_pv_tc_kernel(const __nv_bfloat16
 }
 
 template <int D>
-size_t stats_smem() { return size_t(kRows + kTile) * kRS * 2 + size_t(kThreads / 32) * kVar * kRows * 8; }
+size_t stats_smem() { return size_t(kRows + 2 * kTile) * kRS * 2 + size_t(kThreads / 32) * kVar * kRows * 8; }
 template <int D>
-size_t pv_smem() { return size_t(kRows + 2 * kTile) * kRS * 2 + size_t(kVar) * kRows * (kTile + 8) * 2; }
+size_t pv_smem() { return size_t(kRows + 4 * kTile) * kRS * 2 + size_t(kVar) * kRows * (kTile + 8) * 2; }
 
 }  // namespace tcp
 
