@@ -136,6 +136,7 @@ BF16_CASES = [
     (1, 1, 640, 128, 0.01, 15, "normal"),    # NS = 1
     (1, 1, 700, 128, 1.0, 16, "normal"),     # NS = NT (no corrected blocks)
     (1, 3, 4160, 128, 0.1, 17, "normal"),    # NG = 3
+    (1, 2, 2049, 128, 0.2, 18, "normal"),    # a one-token last block alone in the last group
 ]
 
 
