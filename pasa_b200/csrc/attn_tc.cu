@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* p_ready = s_free + 2;  // [2] set b's P (and U) of its step are in TMEM
   uint64_t* o_done = p_ready + 2;  // [2] the P.V (and correction) MMAs of a step with parity b completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffSlot);
-  __shared__ uint32_t s_nu;
+  __shared__ uint32_t s_nu, s_cnt[2];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 #ifdef PASA_TRACE
@@ -251,6 +251,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       mbar_init(&p_ready[b], kSetWarps); mbar_init(&o_done[b], 1);
     }
     fence_barrier_init();
+    // Q of the tile needs nothing else: it loads while the union list is built
+    mbar_arrive_expect_tx(q_full, C::kQBytes);
+    for (int bx = 0; bx < C::kBoxes; ++bx)
+      tma_load_3d(sm + C::kOffQ + bx * C::kRowBox, &maps.q, q_full, bx * 64, int32_t(pair * kRowsPerTile),
+                  int32_t(bh));
   }
   if (warp == 1) { tmem_alloc(tmem_slot, C::kTmemCols); tmem_relinquish(); }
   if (warp == 0 && lane == 0) {
@@ -269,32 +274,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     }
   }
   __syncthreads();
+  // Union of the two selections, ordered so that consecutive pairs (one
+  // phase-1 step) balance the two halves: blocks only A selected alternate
+  // with blocks only B selected, then the leftover single-half blocks, then
+  // the blocks both selected.  Within each category the order is ascending.
+  // (The softmax is order-independent, so any order gives the same result
+  // up to floating-point rounding.)  Warp 0 counts each category per mask
+  // word and scans the counts over the words; then every thread places
+  // blocks j = tid, tid + kThreads, ... at their positions in parallel.
+  uint32_t* pre = reinterpret_cast<uint32_t*>(xch);  // [3][kMaxNG] exclusive counts (xch is free until the steps)
   if (warp == 0) {
-    // Union of the two selections, ordered so that consecutive pairs (one
-    // phase-1 step) balance the two halves: blocks only A selected alternate
-    // with blocks only B selected, then the leftover single-half blocks, then
-    // the blocks both selected.  Within each category the order is ascending.
-    // (The softmax is order-independent, so any order gives the same result
-    // up to floating-point rounding.)
-    uint32_t na = 0, nb = 0, nboth = 0;
-    for (int64_t w0 = 0; w0 < NG; w0 += 32) {
-      const int64_t w = w0 + lane;
-      const uint32_t ma = (w < NG) ? maskw[w] : 0u, mb = (w < NG) ? maskw[kMaxNG + w] : 0u;
-      na += __popc(ma & ~mb); nb += __popc(mb & ~ma); nboth += __popc(ma & mb);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      na += __shfl_xor_sync(0xffffffffu, na, off);
-      nb += __shfl_xor_sync(0xffffffffu, nb, off);
-      nboth += __shfl_xor_sync(0xffffffffu, nboth, off);
-    }
-    const uint32_t m = na < nb ? na : nb;
     uint32_t ka = 0, kb = 0, kab = 0;  // running counts per category
     for (int64_t w0 = 0; w0 < NG; w0 += 32) {
       const int64_t w = w0 + lane;
       const uint32_t ma = (w < NG) ? maskw[w] : 0u, mb = (w < NG) ? maskw[kMaxNG + w] : 0u;
-      const uint32_t ua = ma & ~mb, ub = mb & ~ma, uab = ma & mb;
-      uint32_t ca = __popc(ua), cb = __popc(ub), cab = __popc(uab);
+      const uint32_t ca = __popc(ma & ~mb), cb = __popc(mb & ~ma), cab = __popc(ma & mb);
       uint32_t ia = ca, ib = cb, iab = cab;  // inclusive scans over lanes
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -303,30 +297,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         const uint32_t yab = __shfl_up_sync(0xffffffffu, iab, off);
         if (lane >= off) { ia += ya; ib += yb; iab += yab; }
       }
-      uint32_t pa = ka + ia - ca, pb = kb + ib - cb, pab = kab + iab - cab;  // category ranks
-      for (uint32_t rem = ua | ub | uab; rem; rem &= rem - 1) {
-        const int bit = __ffs(rem) - 1;
-        const uint32_t j = uint32_t(w * 32 + bit);
-        uint32_t pos;
-        if ((ua >> bit) & 1u) {
-          pos = (pa < m) ? 2 * pa : 2 * m + (pa - m);
-          ++pa;
-          ulist[pos] = uint16_t((j << 2) | 1u);
-        } else if ((ub >> bit) & 1u) {
-          pos = (pb < m) ? 2 * pb + 1 : 2 * m + (na - m) + (pb - m);
-          ++pb;
-          ulist[pos] = uint16_t((j << 2) | 2u);
-        } else {
-          pos = na + nb + pab;
-          ++pab;
-          ulist[pos] = uint16_t((j << 2) | 3u);
-        }
+      if (w < NG) {
+        pre[w] = ka + ia - ca;
+        pre[kMaxNG + w] = kb + ib - cb;
+        pre[2 * kMaxNG + w] = kab + iab - cab;
       }
       ka += __shfl_sync(0xffffffffu, ia, 31);
       kb += __shfl_sync(0xffffffffu, ib, 31);
       kab += __shfl_sync(0xffffffffu, iab, 31);
     }
-    if (lane == 0) s_nu = na + nb + nboth;
+    if (lane == 0) { s_cnt[0] = ka; s_cnt[1] = kb; s_nu = ka + kb + kab; }
+  }
+  __syncthreads();
+  {
+    const uint32_t na = s_cnt[0], nb = s_cnt[1];
+    const uint32_t m = na < nb ? na : nb;
+    for (int64_t j = tid; j < NT; j += kThreads) {
+      const int64_t w = j >> 5;
+      const uint32_t bitm = 1u << (j & 31), below = bitm - 1u;
+      const uint32_t ma = maskw[w], mb = maskw[kMaxNG + w];
+      const uint32_t ua = ma & ~mb, ub = mb & ~ma, uab = ma & mb;
+      if (ua & bitm) {
+        const uint32_t pa = pre[w] + __popc(ua & below);
+        ulist[(pa < m) ? 2 * pa : 2 * m + (pa - m)] = uint16_t((uint32_t(j) << 2) | 1u);
+      } else if (ub & bitm) {
+        const uint32_t pb = pre[kMaxNG + w] + __popc(ub & below);
+        ulist[(pb < m) ? 2 * pb + 1 : 2 * m + (na - m) + (pb - m)] = uint16_t((uint32_t(j) << 2) | 2u);
+      } else if (uab & bitm) {
+        const uint32_t pab = pre[2 * kMaxNG + w] + __popc(uab & below);
+        ulist[na + nb + pab] = uint16_t((uint32_t(j) << 2) | 3u);
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -345,10 +346,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     // ================= TMA producer =================
     if (lane == 0) {
       bool ok = true;
-      const int32_t row0 = int32_t(pair * kRowsPerTile);
-      mbar_arrive_expect_tx(q_full, C::kQBytes);
-      for (int bx = 0; bx < C::kBoxes; ++bx)
-        tma_load_3d(sm + C::kOffQ + bx * C::kRowBox, &maps.q, q_full, bx * 64, row0, int32_t(bh));
       // K and V of phase-1 step p: the two union blocks, each [64 rows] of every 64-column box
       auto load_pair = [&](const CUtensorMap* map, unsigned char* dst, uint64_t* bar, int64_t p) {
         const int32_t j0 = int32_t(ulist[2 * p] >> 2);
