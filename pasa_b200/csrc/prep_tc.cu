@@ -2,12 +2,14 @@
 //
 // Same outputs and rounding points as prep.cu (fused_chunk_reduce +
 // compute_h_group, svg/kernels/triton/group_pisa_attention.py:75-129,
-// :268-301): a CTA owns one (head, group of 32 blocks); k^T v of every block
-// runs on mma.sync (bf16 x bf16 -> fp32, like the reference's tl.dot), the
-// group's sum of bf16(hc_j) stays in registers and h_group is written once.
-// Tiles stream through a two-stage cp.async pipeline so the next block's
-// 48 KB of q, k, v load while the current block computes.  hc itself never
-// reaches HBM.
+// :268-301): a CTA owns one (head, group of 32 blocks), forms k^T v of every
+// block on the tensor core (bf16 x bf16 -> fp32, like the reference's
+// tl.dot), keeps the group's sum of bf16(hc_j) on chip and writes h_group
+// once; hc itself never reaches HBM.  Two kernels:
+//   * prep_tc_kernel (D = 64): k^T v on mma.sync, the group sum in
+//     registers, tiles through a two-stage cp.async pipeline;
+//   * prep_umma_kernel (D = 128, below): TMA tiles, k^T v on tcgen05 into
+//     TMEM, warp-specialised.
 #include <cuda.h>
 
 #include "common.cuh"
