@@ -137,6 +137,8 @@ BF16_CASES = [
     (1, 1, 700, 128, 1.0, 16, "normal"),     # NS = NT (no corrected blocks)
     (1, 3, 4160, 128, 0.1, 17, "normal"),    # NG = 3
     (1, 2, 2049, 128, 0.2, 18, "normal"),    # a one-token last block alone in the last group
+    (1, 1, 50, 128, 0.5, 19, "normal"),      # one partial block: NT = NS = 1, no pair partner
+    (1, 2, 130, 128, 0.5, 20, "normal"),     # NT = 3: a full pair and a lone 2-token block
 ]
 
 
